@@ -1,0 +1,197 @@
+/*
+ * mfm_b200.h — C ABI of the B200-native (sm_100a) modern_fm engine:
+ * sparse-CSR FM / FFM / FwFM scoring and mini-batch training (binary and
+ * multiclass softmax) on NVIDIA B200.
+ *
+ * This ABI replaces the reference's CUDA backend entry points (modern_fm
+ * v1.1.1, Rust crate `modern-fm`). Each function names the reference
+ * interface it stands in for. Plain pointers and sizes only: every array is a
+ * HOST array in the reference's boundary format (float64 values, int64
+ * indices, C-contiguous; rust/src/lib.rs:1-7) unless the name says `_device`.
+ *
+ * Return codes: 0 = success; < 0 = invalid input (the reference raises
+ * ValueError, rust/src/lib.rs:30-32); > 0 = CUDA / device failure (the
+ * reference raises RuntimeError from predict, lib.rs:1510-1512, and ValueError
+ * from fit, lib.rs:437). The message is in mfm_last_error() (thread-local).
+ * No entry point falls back to a CPU path.
+ */
+#ifndef MFM_B200_H
+#define MFM_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MFM_OK 0
+#define MFM_ERR_INVALID (-1)     /* bad shapes / CSR / ids / hyperparameters */
+#define MFM_ERR_UNSUPPORTED (-2) /* valid but outside this engine's limits (e.g. k > 1024) */
+#define MFM_ERR_CUDA 1           /* a CUDA runtime call failed */
+#define MFM_ERR_NO_DEVICE 2      /* no usable CUDA device */
+#define MFM_ERR_DEVICE_CHECK 3   /* a kernel's own bounds / status check fired */
+
+enum { MFM_DTYPE_F64 = 0, MFM_DTYPE_F32 = 1 };
+enum { MFM_LOSS_LOGISTIC = 0, MFM_LOSS_SQUARED = 1 };
+enum { MFM_OPT_SGD = 0, MFM_OPT_ADAGRAD = 1, MFM_OPT_ADAM = 2, MFM_OPT_FTRL = 3 };
+
+/* CSR matrix (scipy indptr/indices/data), host memory.
+ * Stands in for CsrView (rust/src/data.rs:7-11). */
+typedef struct {
+    const int64_t* indptr;  /* n_rows + 1 */
+    const int64_t* indices; /* nnz */
+    const double* data;     /* nnz */
+    int64_t n_rows;
+    int64_t nnz;
+    int64_t n_features;
+} mfm_csr;
+
+/* Execution options. dtype selects the device arithmetic type of parameters,
+ * sums and optimizer state (float64 reproduces the reference's float64
+ * arithmetic; float32 halves the bytes every gather moves). device is the
+ * first CUDA ordinal; predict shards rows over n_devices devices. */
+typedef struct {
+    int dtype;
+    int device;
+    int n_devices;
+} mfm_exec;
+
+/* Training configuration: the scalar arguments of the reference's fit entry
+ * points (rust/src/lib.rs:283-322) plus row_orders (n_epochs, n_rows). */
+typedef struct {
+    int loss;      /* MFM_LOSS_* (binary only) */
+    int optimizer; /* MFM_OPT_* */
+    double learning_rate, l1_linear, l2_linear, l1_factors, l2_factors;
+    double beta_1, beta_2, epsilon, ftrl_beta, label_smoothing;
+    const int64_t* row_orders;
+    int64_t n_epochs;
+    int64_t batch_size;
+} mfm_train;
+
+/* One parameter group (w0, w, V or R) and its optimizer state, all read and
+ * written in place. acc = AdaGrad accumulator; (m, s, t) = Adam; (z, n) =
+ * FTRL. A NULL state pointer means "not provided": the engine keeps a zeroed
+ * device-side state for the duration of the call, exactly as the reference
+ * does with its local_state (rust/src/lib.rs:79-87). For binary models the w0
+ * group points at scalars. */
+typedef struct {
+    double* param;
+    double* acc;
+    double* m;
+    double* s;
+    double* t;
+    double* z;
+    double* n;
+} mfm_group;
+
+/* Replaces cuda::available() / has_cuda (rust/src/cuda/mod.rs:38-44,
+ * rust/src/lib.rs:1471-1482): 1 when a CUDA device is usable. */
+int mfm_has_cuda(void);
+
+/* Thread-local message for the last non-zero return code. */
+const char* mfm_last_error(void);
+
+/* Number of CUDA devices visible to the process (0 when none). */
+int mfm_device_count(void);
+
+/* ---- prediction (transfer-inclusive, like the reference) ---------------- */
+
+/* Replaces fm_predict_cuda_csr -> cuda::fm::predict_csr
+ * (rust/src/lib.rs:1488-1513, rust/src/cuda/fm.rs:61-109).
+ * w: (n_features), v: (n_features, k), out: (n_rows). */
+int mfm_fm_predict_csr(const mfm_csr* x, double w0, const double* w, const double* v,
+                       int64_t k, double* out, const mfm_exec* ex);
+
+/* Replaces ffm_predict_cuda_csr -> cuda::ffm::predict_csr
+ * (rust/src/lib.rs:1519-1548, rust/src/cuda/ffm.rs:81-136).
+ * field_ids: (n_features), v: (n_features, n_fields, k). */
+int mfm_ffm_predict_csr(const mfm_csr* x, const int64_t* field_ids, int64_t n_fields,
+                        double w0, const double* w, const double* v, int64_t k, double* out,
+                        const mfm_exec* ex);
+
+/* Replaces fwfm_predict_cuda_csr -> cuda::fwfm::predict_csr
+ * (rust/src/lib.rs:1554-1590, rust/src/cuda/fwfm.rs:77-135).
+ * v: (n_features, k), r: (n_fields, n_fields), upper triangle read. */
+int mfm_fwfm_predict_csr(const mfm_csr* x, const int64_t* field_ids, int64_t n_fields,
+                         double w0, const double* w, const double* v, const double* r,
+                         int64_t k, double* out, const mfm_exec* ex);
+
+/* ---- training (whole fit call device-resident) --------------------------- */
+
+/* Replaces fm_fit_csr(use_cuda=True) -> cuda::fm_train::fit_csr
+ * (rust/src/lib.rs:283-439, rust/src/cuda/fm_train.rs:175-444).
+ * Groups: w0 (scalar), w (n_features), v (n_features, k). */
+int mfm_fm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                   const mfm_train* tr, int64_t k, mfm_group* w0, mfm_group* w, mfm_group* v,
+                   const mfm_exec* ex);
+
+/* Replaces fm_fit_multiclass_csr(use_cuda=True) -> cuda::fm_train_mc
+ * (rust/src/lib.rs:449-630, rust/src/cuda/fm_train_mc.rs:163-472).
+ * y: class ids (n_rows). Groups: w0 (C), w (C, n_features), v (C, n_features, k). */
+int mfm_fm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                              const double* sample_weight, int64_t n_classes,
+                              const mfm_train* tr, int64_t k, mfm_group* w0, mfm_group* w,
+                              mfm_group* v, const mfm_exec* ex);
+
+/* Replaces ffm_fit_csr(use_cuda=True) -> cuda::ffm_train::fit_csr
+ * (rust/src/lib.rs:635-793, rust/src/cuda/ffm_train.rs:197-436).
+ * v: (n_features, n_fields, k). */
+int mfm_ffm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                    const int64_t* field_ids, int64_t n_fields, const mfm_train* tr,
+                    int64_t k, mfm_group* w0, mfm_group* w, mfm_group* v,
+                    const mfm_exec* ex);
+
+/* Replaces ffm_fit_multiclass_csr(use_cuda=True) -> cuda::ffm_train_mc
+ * (rust/src/lib.rs:800-978, rust/src/cuda/ffm_train_mc.rs:198-515).
+ * v: (C, n_features, n_fields, k). */
+int mfm_ffm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                               const double* sample_weight, int64_t n_classes,
+                               const int64_t* field_ids, int64_t n_fields,
+                               const mfm_train* tr, int64_t k, mfm_group* w0, mfm_group* w,
+                               mfm_group* v, const mfm_exec* ex);
+
+/* Replaces fwfm_fit_csr(use_cuda=True) -> cuda::fwfm_train::fit_csr
+ * (rust/src/lib.rs:1049-1242, rust/src/cuda/fwfm_train.rs:314-610).
+ * v: (n_features, k), r: (n_fields, n_fields). */
+int mfm_fwfm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                     const int64_t* field_ids, int64_t n_fields, const mfm_train* tr,
+                     int64_t k, mfm_group* w0, mfm_group* w, mfm_group* v, mfm_group* r,
+                     const mfm_exec* ex);
+
+/* Replaces fwfm_fit_multiclass_csr(use_cuda=True) -> cuda::fwfm_train
+ * (rust/src/lib.rs:1249-1466, rust/src/cuda/fwfm_train.rs:615-955).
+ * v: (C, n_features, k), r: (C, n_fields, n_fields). */
+int mfm_fwfm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                                const double* sample_weight, int64_t n_classes,
+                                const int64_t* field_ids, int64_t n_fields,
+                                const mfm_train* tr, int64_t k, mfm_group* w0, mfm_group* w,
+                                mfm_group* v, mfm_group* r, const mfm_exec* ex);
+
+/* ---- device-resident prediction (no reference counterpart) -------------
+ * Every pointer is DEVICE memory on `device`, already in the compute layout:
+ * indptr int64 (n_rows+1), indices int32, data/w/v/r/out in `dtype`
+ * (float or double). `stream` is a cudaStream_t (NULL = legacy default).
+ * No host<->device copies, no allocation, no validation beyond sizes: the
+ * caller guarantees the CSR is canonical and in range. Used for
+ * device-resident throughput and by callers that keep data on the GPU. */
+int mfm_fm_predict_device(int dtype, int device, const int64_t* indptr,
+                          const int32_t* indices, const void* data, int64_t n_rows,
+                          double w0, const void* w, const void* v, int64_t k, void* out,
+                          void* stream);
+int mfm_ffm_predict_device(int dtype, int device, const int64_t* indptr,
+                           const int32_t* indices, const void* data, int64_t n_rows,
+                           const int32_t* field_ids, int64_t n_fields, double w0,
+                           const void* w, const void* v, int64_t k, void* out, void* stream);
+int mfm_fwfm_predict_device(int dtype, int device, const int64_t* indptr,
+                            const int32_t* indices, const void* data, int64_t n_rows,
+                            const int32_t* field_ids, int64_t n_fields, double w0,
+                            const void* w, const void* v, const void* r, int64_t k, void* out,
+                            void* stream);
+
+/* Release the engine's cached device memory on every device. */
+void mfm_release_cached_memory(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

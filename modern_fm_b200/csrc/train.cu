@@ -1,0 +1,1273 @@
+// train.cu — device-resident mini-batch training for FM, FFM and FwFM
+// (binary and multiclass softmax) on sm_100a, replacing the reference's
+// cuda::{fm,ffm,fwfm}_train[_mc] host loops (rust/src/cuda/*_train*.rs), which
+// accumulate with float atomics on the GPU and then download every batch's
+// gradient for a CPU optimizer flush.
+//
+// Semantics follow the reference's CPU engine (rust/src/{fm,ffm,fwfm}.rs):
+// every batch (a contiguous chunk of row_orders[e]) computes per-row gradients
+// from the frozen batch-start parameters, sums them per touched coordinate,
+// divides by the batch length and applies one optimizer step per touched
+// coordinate (lazy L2; update sets: features for w and FM/FwFM V, (feature,
+// field) slots hit by a pair for FFM V, hit field pairs for FwFM R; w0 always).
+//
+// Device pipeline (no float atomics, bitwise reproducible run to run):
+//   per epoch, for each entry stream (FEAT: one entry per nonzero keyed by
+//   feature; SLOT: one per ordered pair keyed by FFM slot; PAIR: one per
+//   unordered pair keyed by FwFM field pair):
+//     count -> scan -> expand (key, batch-local entry id) -> segmented stable
+//     radix sort by key within each batch -> run detection -> work items of
+//     <= kItem entries per run;
+//   per batch:
+//     forward kernel (warp per row): scores, loss gradient, per-entry gradient
+//       payloads (all classes);
+//     stage 1 (warp per work item): sums payload rows of its entries in sorted
+//       order; single-item runs apply the optimizer at once;
+//     stage 2 (warp per multi-item run): combines item partials in order and
+//       applies; one extra block steps w0 from the per-row gradients.
+#include <algorithm>
+#include <cmath>
+
+#include "segsort.cuh"
+
+namespace mfm {
+
+constexpr int kItem = 32;  // entries per reduction work item (one warp)
+enum StreamKind { FEAT = 0, SLOT = 1, PAIR = 2 };
+enum Model { M_FM = 0, M_FFM = 1, M_FWFM = 2 };
+
+// ------------------------------------------------------------ optimizer --
+
+template <class T>
+struct GroupDev {
+    T *p, *acc, *m, *s, *t, *z, *n;
+    int64_t width;  // parameters per key (per row of the device layout)
+    int reg;        // 0 linear (l1/l2_linear), 1 factors, 2 none (w0)
+};
+
+struct OptDev {
+    int kind;
+    double lr, b1, b2, eps, fbeta;
+    double l1[3], l2[3];
+};
+
+// One step of the reference's step_param / step_coord (rust/src/optimizer.rs:
+// 48-167) for coordinate idx of group g with batch-mean data gradient dg.
+template <class T>
+__device__ __forceinline__ void opt_step(const GroupDev<T>& g, int64_t idx, T dg,
+                                         const OptDev& o) {
+    T th = g.p[idx];
+    const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
+    switch (o.kind) {
+    case MFM_OPT_SGD:  // apply_update, optimizer.rs:48-60
+        th -= lr * (dg + l2 * th);
+        break;
+    case MFM_OPT_ADAGRAD: {
+        const T gr = dg + l2 * th;
+        const T a = g.acc[idx] + gr * gr;
+        g.acc[idx] = a;
+        th -= lr * gr / sqrt(a + (T)1e-10);
+        break;
+    }
+    case MFM_OPT_ADAM: {  // adam_step, optimizer.rs:68-85 (lazy, per-coordinate t)
+        const T gr = dg + l2 * th;
+        const T b1 = (T)o.b1, b2 = (T)o.b2;
+        const T t = g.t[idx] + T(1);
+        const T m = b1 * g.m[idx] + (T(1) - b1) * gr;
+        const T v = b2 * g.s[idx] + (T(1) - b2) * gr * gr;
+        g.t[idx] = t;
+        g.m[idx] = m;
+        g.s[idx] = v;
+        const T mh = m / (T(1) - pow(b1, t));
+        const T vh = v / (T(1) - pow(b2, t));
+        th -= lr * mh / (sqrt(vh) + (T)o.eps);
+        break;
+    }
+    default: {  // FTRL-Proximal, ftrl_step, optimizer.rs:93-105 (pure data gradient)
+        const T n = g.n[idx];
+        const T nn = n + dg * dg;
+        const T sigma = (sqrt(nn) - sqrt(n)) / lr;
+        const T z = g.z[idx] + dg - sigma * th;
+        g.z[idx] = z;
+        g.n[idx] = nn;
+        if (fabs(z) <= l1)
+            th = T(0);
+        else {
+            const T sign = z < T(0) ? T(-1) : T(1);
+            th = -(z - sign * l1) / (((T)o.fbeta + sqrt(nn)) / lr + l2);
+        }
+    }
+    }
+    g.p[idx] = th;
+}
+
+// --------------------------------------------------------- layout moves --
+
+// src (C, R, K) float64 row-major <-> dst (R, C, K) in T: the device keeps
+// every key's classes contiguous (one gather per key); C = 1 is a plain copy.
+template <class T>
+__global__ void to_device_layout(const double* __restrict__ src, T* __restrict__ dst,
+                                 int64_t C, int64_t R, int64_t K) {
+    const int64_t total = C * R * K, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t r = i / (C * K), rem = i - r * C * K, c = rem / K, kk = rem - c * K;
+        dst[i] = (T)src[(c * R + r) * K + kk];
+    }
+}
+template <class T>
+__global__ void from_device_layout(const T* __restrict__ src, double* __restrict__ dst,
+                                   int64_t C, int64_t R, int64_t K) {
+    const int64_t total = C * R * K, stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const int64_t r = i / (C * K), rem = i - r * C * K, c = rem / K, kk = rem - c * K;
+        dst[(c * R + r) * K + kk] = (double)src[i];
+    }
+}
+template <class Tin, class Tout>
+__global__ void convert_kernel(const Tin* __restrict__ src, Tout* __restrict__ dst, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = (Tout)src[i];
+}
+
+// ------------------------------------------------------- epoch planning --
+
+__device__ __forceinline__ int64_t stream_count(int kind, int64_t z) {
+    return kind == FEAT ? z : (kind == SLOT ? z * (z - 1) : z * (z - 1) / 2);
+}
+
+__global__ void count_kernel(int kind, const int32_t* __restrict__ order,
+                             const int64_t* __restrict__ indptr, int64_t n_rows,
+                             int64_t* __restrict__ cnt) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows) return;
+    const int64_t row = order[i];
+    cnt[i] = stream_count(kind, indptr[row + 1] - indptr[row]);
+}
+
+__global__ void seg_lo_kernel(const int64_t* __restrict__ estart, int64_t n_rows, int64_t B,
+                              int64_t nb, int64_t* __restrict__ seg_lo) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b > nb) return;
+    const int64_t pos = b * B < n_rows ? b * B : n_rows;
+    seg_lo[b] = estart[pos];
+}
+
+__device__ __forceinline__ void pair_step(int64_t& a, int64_t& b, int64_t z) {
+    while (a < z - 1 && b >= z) {
+        b = b - z + a + 2;
+        ++a;
+    }
+}
+
+// One warp per epoch position: writes the keys and batch-local entry ids of
+// the row's entries, in the order the forward kernel writes their payloads.
+__global__ void __launch_bounds__(256)
+    expand_kernel(int kind, const int32_t* __restrict__ order, const int64_t* __restrict__ indptr,
+                  const int32_t* __restrict__ indices, const int32_t* __restrict__ fid, int F,
+                  int64_t n_rows, int64_t B, const int64_t* __restrict__ estart,
+                  const int64_t* __restrict__ seg_lo, uint32_t* __restrict__ keys,
+                  uint32_t* __restrict__ vals) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t pos = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; pos < n_rows;
+         pos += nwarps) {
+        const int64_t row = order[pos];
+        const int64_t rb = indptr[row], z = indptr[row + 1] - rb;
+        const int32_t* ix = indices + rb;
+        const int64_t base = estart[pos];
+        const int64_t local = base - seg_lo[pos / B];
+        if (kind == FEAT) {
+            for (int64_t a = lane; a < z; a += 32) {
+                keys[base + a] = (uint32_t)ix[a];
+                vals[base + a] = (uint32_t)(local + a);
+            }
+        } else if (kind == SLOT) {  // ordered pairs (a, b != a): key = i_a * F + f_b
+            const int64_t tot = z * (z - 1);
+            for (int64_t q = lane; q < tot; q += 32) {
+                const int64_t a = q / (z - 1), bi = q - a * (z - 1), b = bi < a ? bi : bi + 1;
+                keys[base + q] = (uint32_t)((int64_t)ix[a] * F + fid[ix[b]]);
+                vals[base + q] = (uint32_t)(local + q);
+            }
+        } else {  // unordered pairs a < b: key = pair_slot(f_a, f_b)
+            int64_t a = 0, b = 1 + lane, pi = lane;
+            pair_step(a, b, z);
+            while (a < z - 1) {
+                const int fa = fid[ix[a]], fb = fid[ix[b]];
+                keys[base + pi] = (uint32_t)(fa <= fb ? fa * F + fb : fb * F + fa);
+                vals[base + pi] = (uint32_t)(local + pi);
+                b += 32;
+                pi += 32;
+                pair_step(a, b, z);
+            }
+        }
+    }
+}
+
+__global__ void head_kernel(const uint32_t* __restrict__ keys, int64_t n,
+                            int32_t* __restrict__ head) {
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p < n) head[p] = (p == 0 || keys[p] != keys[p - 1]) ? 1 : 0;
+}
+__global__ void seg_head_kernel(const int64_t* __restrict__ seg_lo, int64_t nb,
+                                int32_t* __restrict__ head) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < nb && seg_lo[b] < seg_lo[b + 1]) head[seg_lo[b]] = 1;
+}
+__global__ void run_start_kernel(const int32_t* __restrict__ head,
+                                 const int64_t* __restrict__ run_id, int64_t n,
+                                 int64_t* __restrict__ run_start) {
+    const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p < n && head[p]) run_start[run_id[p]] = p;
+    if (p == 0) run_start[run_id[n]] = n;
+}
+__global__ void pieces_kernel(const int64_t* __restrict__ run_start, int64_t R,
+                              int64_t* __restrict__ np, int64_t* __restrict__ longf) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int64_t c = ceil_div(run_start[r + 1] - run_start[r], kItem);
+    np[r] = c;
+    longf[r] = c > 1 ? 1 : 0;
+}
+__global__ void items_kernel(const int64_t* __restrict__ item_start,
+                             const int64_t* __restrict__ long_scan, int64_t R,
+                             int64_t* __restrict__ item_run, int64_t* __restrict__ long_list) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int64_t i0 = item_start[r], i1 = item_start[r + 1];
+    for (int64_t i = i0; i < i1; ++i) item_run[i] = r;
+    if (i1 - i0 > 1) long_list[long_scan[r]] = r;
+}
+__global__ void batch_tables_kernel(const int64_t* __restrict__ seg_lo, int64_t nb,
+                                    const int64_t* __restrict__ run_id,
+                                    const int64_t* __restrict__ item_start,
+                                    const int64_t* __restrict__ long_scan,
+                                    int64_t* __restrict__ bitem, int64_t* __restrict__ blong) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b > nb) return;
+    const int64_t r = run_id[seg_lo[b]];
+    bitem[b] = item_start[r];
+    blong[b] = long_scan[r];
+}
+
+// ------------------------------------------------------ forward kernels --
+
+template <class T>
+struct FwdArgs {
+    const int64_t* indptr;
+    const int32_t* indices;
+    const T* data;
+    const int32_t* order;  // row_orders[e]
+    int64_t pos0, nrows;   // this batch: epoch positions [pos0, pos0 + nrows)
+    const int64_t* estart1;
+    int64_t seg1;  // stream 1 (FEAT) entry start per position; batch start
+    const int64_t* estart2;
+    int64_t seg2;  // stream 2 (SLOT / PAIR)
+    const T* y;
+    const int32_t* ycls;
+    const T* sw;
+    int C, k, F, loss, multiclass;
+    T ls_on, ls_off;  // softmax targets: 1 - eps for the true class, eps / (C - 1) otherwise
+    const T *w0, *w, *v, *r;
+    const int32_t* fid;
+    T* pay1;
+    int W1;
+    T* pay2;
+    int W2;
+    T* grow;  // (nrows, C) per-row loss gradients, summed into the w0 gradient
+};
+
+template <class T>
+__device__ __forceinline__ T sigmoid_t(T s) {  // optimizer.rs:28-35
+    if (s >= T(0)) return T(1) / (T(1) + exp(-s));
+    const T e = exp(s);
+    return e / (T(1) + e);
+}
+
+// lane 0: per-class gradients of one row from its logits (sm_logit) into sm_g.
+template <class T>
+__device__ __forceinline__ void row_gradients(const FwdArgs<T>& A, int64_t row, const T* lg,
+                                              T* g) {
+    const T sw = A.sw[row];
+    if (!A.multiclass) {  // loss_grad, optimizer.rs:38-43
+        const T s = lg[0], y = A.y[row];
+        g[0] = sw * (A.loss == MFM_LOSS_LOGISTIC ? sigmoid_t(s) - y : s - y);
+        return;
+    }
+    // stable softmax with label smoothing, rust/src/fm.rs:357-393
+    T mx = -INFINITY;
+    for (int c = 0; c < A.C; ++c) mx = fmax(mx, lg[c]);
+    T sum = T(0);
+    for (int c = 0; c < A.C; ++c) {
+        g[c] = exp(lg[c] - mx);
+        sum += g[c];
+    }
+    const int yc = A.ycls[row];
+    for (int c = 0; c < A.C; ++c) {
+        const T p = g[c] / sum;
+        g[c] = sw * (p - (c == yc ? A.ls_on : A.ls_off));
+    }
+}
+
+// FM (binary and multiclass): D = C*k latent columns per feature, split over
+// Lc lanes (G = 32/Lc nonzeros per warp step), MCOL columns per lane.
+// Payload per nonzero: [g_c x (C) | g_c (x cache_cf - v_cf x^2) (C*k)]
+// (FmGradAccum::add_row, rust/src/fm.rs:133-146).
+template <class T, int MCOL>
+__global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) {
+    extern __shared__ unsigned char smraw[];
+    const int C = A.C, k = A.k, D = C * k;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    T* sm = reinterpret_cast<T*>(smraw) + (size_t)wib * (D + 3 * C);
+    T *colv = sm, *lins = sm + D, *logit = lins + C, *gs = logit + C;
+    const int Lc = 1 << lgc, G = 32 >> lgc, grp = lane >> lgc, l = lane & (Lc - 1);
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
+         j += nwarps) {
+        const int64_t pos = A.pos0 + j, row = A.order[pos];
+        const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
+        T cache[MCOL], sq[MCOL];
+#pragma unroll
+        for (int m = 0; m < MCOL; ++m) cache[m] = sq[m] = T(0);
+        T lin = T(0);
+        for (int64_t base = 0; base < z; base += 32) {
+            const int nh = (int)min((int64_t)32, z - base);
+            int32_t my_i = 0;
+            T my_x = T(0);
+            if (lane < nh) {
+                my_i = A.indices[rb + base + lane];
+                my_x = A.data[rb + base + lane];
+            }
+            for (int t = 0; t < nh; t += G) {
+                const int src = t + grp;
+                const int32_t i = __shfl_sync(0xffffffffu, my_i, src);
+                const T x = __shfl_sync(0xffffffffu, my_x, src);
+                if (src < nh) {
+                    const T* vi = A.v + (int64_t)i * D;
+#pragma unroll
+                    for (int m = 0; m < MCOL; ++m) {
+                        const int jj = l + m * Lc;
+                        if (jj < D) {
+                            const T vx = vi[jj] * x;
+                            cache[m] += vx;
+                            sq[m] += vx * vx;
+                        }
+                    }
+                    if (l < C) lin += A.w[(int64_t)i * C + l] * x;
+                }
+            }
+        }
+        for (int o = Lc; o < 32; o <<= 1) {
+#pragma unroll
+            for (int m = 0; m < MCOL; ++m) {
+                cache[m] += __shfl_xor_sync(0xffffffffu, cache[m], o);
+                sq[m] += __shfl_xor_sync(0xffffffffu, sq[m], o);
+            }
+            lin += __shfl_xor_sync(0xffffffffu, lin, o);
+        }
+        if (grp == 0) {
+#pragma unroll
+            for (int m = 0; m < MCOL; ++m) {
+                const int jj = l + m * Lc;
+                if (jj < D) colv[jj] = cache[m] * cache[m] - sq[m];
+            }
+            if (l < C) lins[l] = lin;
+        }
+        __syncwarp();
+        for (int c = lane; c < C; c += 32) {
+            T s = T(0);
+            for (int t = 0; t < k; ++t) s += colv[c * k + t];
+            logit[c] = A.w0[c] + lins[c] + T(0.5) * s;
+        }
+        __syncwarp();
+        if (lane == 0) row_gradients(A, row, logit, gs);
+        __syncwarp();
+        for (int c = lane; c < C; c += 32) A.grow[j * C + c] = gs[c];
+        // payload rows of this row's nonzeros (batch-local entry ids)
+        const int64_t e0 = A.estart1[pos] - A.seg1;
+        for (int64_t base = 0; base < z; base += 32) {
+            const int nh = (int)min((int64_t)32, z - base);
+            int32_t my_i = 0;
+            T my_x = T(0);
+            if (lane < nh) {
+                my_i = A.indices[rb + base + lane];
+                my_x = A.data[rb + base + lane];
+            }
+            for (int t = 0; t < nh; t += G) {
+                const int src = t + grp;
+                const int32_t i = __shfl_sync(0xffffffffu, my_i, src);
+                const T x = __shfl_sync(0xffffffffu, my_x, src);
+                if (src < nh) {
+                    const T* vi = A.v + (int64_t)i * D;
+                    T* P = A.pay1 + (e0 + base + src) * A.W1;
+                    if (l < C) P[l] = gs[l] * x;
+#pragma unroll
+                    for (int m = 0; m < MCOL; ++m) {
+                        const int jj = l + m * Lc;
+                        if (jj < D) P[C + jj] = gs[jj / k] * (x * cache[m] - vi[jj] * x * x);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// FFM (binary and multiclass). Device V layout (n, F, C, k).
+// Stream 1 (FEAT) payload: [g_c x_a] (w gradient);
+// stream 2 (SLOT) payload per ordered pair (a, b != a), slot (i_a, f_b):
+// [g_c x_a x_b V[i_b, f_a, c, :]] (FfmGradAccum::add_row, rust/src/ffm.rs:129-171).
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
+    extern __shared__ unsigned char smraw[];
+    const int C = A.C, k = A.k, F = A.F, CK = C * k;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    T* logit = reinterpret_cast<T*>(smraw) + (size_t)wib * 2 * C;
+    T* gs = logit + C;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
+         j += nwarps) {
+        const int64_t pos = A.pos0 + j, row = A.order[pos];
+        const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
+        const int32_t* ix = A.indices + rb;
+        const T* dv = A.data + rb;
+        for (int c = 0; c < C; ++c) {  // ffm_score_row, rust/src/ffm.rs:18-45
+            T acc = T(0);
+            for (int64_t q = lane; q < z; q += 32) acc += A.w[(int64_t)ix[q] * C + c] * dv[q];
+            int64_t a = 0, b = 1 + lane;
+            pair_step(a, b, z);
+            while (a < z - 1) {
+                const int32_t ia = ix[a], ib = ix[b];
+                const int fa = A.fid[ia], fb = A.fid[ib];
+                const T* pa = A.v + (((int64_t)ia * F + fb) * C + c) * k;
+                const T* pb = A.v + (((int64_t)ib * F + fa) * C + c) * k;
+                T dot = T(0);
+                for (int t = 0; t < k; t += VEC) {
+                    const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) dot += qa.v[u] * qb.v[u];
+                }
+                acc += dot * dv[a] * dv[b];
+                b += 32;
+                pair_step(a, b, z);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) logit[c] = A.w0[c] + acc;
+        }
+        __syncwarp();
+        if (lane == 0) row_gradients(A, row, logit, gs);
+        __syncwarp();
+        for (int c = lane; c < C; c += 32) A.grow[j * C + c] = gs[c];
+        const int64_t e1 = A.estart1[pos] - A.seg1;
+        for (int64_t q = lane; q < z * C; q += 32) {
+            const int64_t a = q / C;
+            const int c = (int)(q - a * C);
+            A.pay1[(e1 + a) * C + c] = gs[c] * dv[a];
+        }
+        const int64_t e2 = A.estart2[pos] - A.seg2;
+        const int64_t tot = z * (z - 1) * CK;
+        for (int64_t q = lane; q < tot; q += 32) {
+            const int64_t pe = q / CK;
+            const int col = (int)(q - pe * CK);
+            const int64_t a = pe / (z - 1), bi = pe - a * (z - 1), b = bi < a ? bi : bi + 1;
+            const int c = col / k, t = col - c * k;
+            const int32_t ib = ix[b];
+            const int fa = A.fid[ix[a]];
+            A.pay2[(e2 + pe) * CK + col] =
+                gs[c] * dv[a] * dv[b] * A.v[(((int64_t)ib * F + fa) * C + c) * k + t];
+        }
+        __syncwarp();
+    }
+}
+
+// FwFM (binary and multiclass). Device layouts: V (n, C, k), R (F*F, C).
+// Stream 1 (FEAT) payload per nonzero a: [g_c x_a | g_c x_a sum_{b!=a}
+// r_c(f_a,f_b) x_b v_{b,c,:}]; stream 2 (PAIR) payload per pair a < b:
+// [g_c x_a x_b <v_a,c, v_b,c>] (FwfmGradAccum::add_row, rust/src/fwfm.rs:140-183).
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
+    extern __shared__ unsigned char smraw[];
+    const int C = A.C, k = A.k, F = A.F, W1 = A.W1;
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    T* logit = reinterpret_cast<T*>(smraw) + (size_t)wib * 2 * C;
+    T* gs = logit + C;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
+         j += nwarps) {
+        const int64_t pos = A.pos0 + j, row = A.order[pos];
+        const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
+        const int32_t* ix = A.indices + rb;
+        const T* dv = A.data + rb;
+        for (int c = 0; c < C; ++c) {  // fwfm_score_row, rust/src/fwfm.rs:24-53
+            T acc = T(0);
+            for (int64_t q = lane; q < z; q += 32) acc += A.w[(int64_t)ix[q] * C + c] * dv[q];
+            int64_t a = 0, b = 1 + lane;
+            pair_step(a, b, z);
+            while (a < z - 1) {
+                const int32_t ia = ix[a], ib = ix[b];
+                const int fa = A.fid[ia], fb = A.fid[ib];
+                const T rw = A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
+                const T* pa = A.v + ((int64_t)ia * C + c) * k;
+                const T* pb = A.v + ((int64_t)ib * C + c) * k;
+                T dot = T(0);
+                for (int t = 0; t < k; t += VEC) {
+                    const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) dot += qa.v[u] * qb.v[u];
+                }
+                acc += rw * dot * dv[a] * dv[b];
+                b += 32;
+                pair_step(a, b, z);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) logit[c] = A.w0[c] + acc;
+        }
+        __syncwarp();
+        if (lane == 0) row_gradients(A, row, logit, gs);
+        __syncwarp();
+        for (int c = lane; c < C; c += 32) A.grow[j * C + c] = gs[c];
+        const int64_t e1 = A.estart1[pos] - A.seg1;
+        for (int64_t q = lane; q < z * W1; q += 32) {
+            const int64_t a = q / W1;
+            const int col = (int)(q - a * W1);
+            T val;
+            if (col < C) {
+                val = gs[col] * dv[a];
+            } else {
+                const int jj = col - C, c = jj / k, t = jj - c * k;
+                const int fa = A.fid[ix[a]];
+                T s = T(0);
+                for (int64_t b = 0; b < z; ++b) {
+                    if (b == a) continue;
+                    const int32_t ib = ix[b];
+                    const int fb = A.fid[ib];
+                    const T rw = A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
+                    s += rw * dv[b] * A.v[((int64_t)ib * C + c) * k + t];
+                }
+                val = gs[c] * dv[a] * s;
+            }
+            A.pay1[(e1 + a) * W1 + col] = val;
+        }
+        const int64_t e2 = A.estart2[pos] - A.seg2;
+        int64_t a = 0, b = 1 + lane, pi = lane;
+        pair_step(a, b, z);
+        while (a < z - 1) {
+            const int32_t ia = ix[a], ib = ix[b];
+            const T xab = dv[a] * dv[b];
+            for (int c = 0; c < C; ++c) {
+                const T* pa = A.v + ((int64_t)ia * C + c) * k;
+                const T* pb = A.v + ((int64_t)ib * C + c) * k;
+                T dot = T(0);
+                for (int t = 0; t < k; ++t) dot += pa[t] * pb[t];
+                A.pay2[(e2 + pi) * C + c] = gs[c] * xab * dot;
+            }
+            b += 32;
+            pi += 32;
+            pair_step(a, b, z);
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------- reduce + optimizer --
+
+template <class T>
+struct RedArgs {
+    const uint32_t* keys;  // sorted keys of the epoch
+    const uint32_t* vals;  // batch-local entry ids, in sorted order
+    const int64_t* run_start;
+    const int64_t* item_start;
+    const int64_t* item_run;
+    const int64_t* long_list;
+    const T* pay;
+    T* part;
+    int W;
+    int cb1;  // first column of group 1 (== W when there is one group)
+    GroupDev<T> g0, g1;
+    OptDev opt;
+    T inv_bsz;
+};
+
+template <class T>
+__device__ __forceinline__ void apply_col(const RedArgs<T>& R, uint32_t key, int col, T sum) {
+    if (col < R.cb1)
+        opt_step(R.g0, (int64_t)key * R.g0.width + col, sum * R.inv_bsz, R.opt);
+    else
+        opt_step(R.g1, (int64_t)key * R.g1.width + (col - R.cb1), sum * R.inv_bsz, R.opt);
+}
+
+// Stage 1: one warp per work item (<= kItem sorted entries of one run).
+template <class T, int MW>
+__global__ void __launch_bounds__(256)
+    reduce_stage1_kernel(RedArgs<T> R, int64_t item0, int64_t item1) {
+    const int lane = threadIdx.x & 31;
+    const int64_t it = item0 + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (it >= item1) return;
+    const int64_t r = R.item_run[it];
+    const int64_t i0 = R.item_start[r], npieces = R.item_start[r + 1] - i0;
+    const int64_t rs = R.run_start[r], re = R.run_start[r + 1];
+    const int64_t p0 = rs + (it - i0) * kItem;
+    const int cnt = (int)min((int64_t)kItem, re - p0);
+    const uint32_t key = R.keys[rs];
+    const uint32_t my_e = lane < cnt ? R.vals[p0 + lane] : 0u;
+    for (int cb = 0; cb < R.W; cb += 32 * MW) {
+        T acc[MW];
+#pragma unroll
+        for (int m = 0; m < MW; ++m) acc[m] = T(0);
+#pragma unroll 4
+        for (int q = 0; q < cnt; ++q) {
+            const T* row = R.pay + (int64_t)__shfl_sync(0xffffffffu, my_e, q) * R.W;
+#pragma unroll
+            for (int m = 0; m < MW; ++m) {
+                const int col = cb + lane + 32 * m;
+                if (col < R.W) acc[m] += row[col];
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MW; ++m) {
+            const int col = cb + lane + 32 * m;
+            if (col >= R.W) continue;
+            if (npieces == 1)
+                apply_col(R, key, col, acc[m]);
+            else
+                R.part[(it - item0) * R.W + col] = acc[m];
+        }
+    }
+}
+
+// Stage 2: one warp per run longer than kItem: item partials in order.
+template <class T>
+__global__ void __launch_bounds__(256)
+    reduce_stage2_kernel(RedArgs<T> R, int64_t long0, int64_t long1, int64_t item0) {
+    const int lane = threadIdx.x & 31;
+    const int64_t li = long0 + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+    if (li >= long1) return;
+    const int64_t r = R.long_list[li];
+    const int64_t i0 = R.item_start[r], i1 = R.item_start[r + 1];
+    const uint32_t key = R.keys[R.run_start[r]];
+    for (int col = lane; col < R.W; col += 32) {
+        T s = T(0);
+        for (int64_t it = i0; it < i1; ++it) s += R.part[(it - item0) * R.W + col];
+        apply_col(R, key, col, s);
+    }
+}
+
+// w0: the batch's per-row gradients summed in a fixed tree, then one step.
+template <class T>
+__global__ void __launch_bounds__(256)
+    w0_kernel(const T* __restrict__ grow, int64_t nrows, int C, GroupDev<T> g, OptDev o,
+              T inv_bsz) {
+    __shared__ T sm[256];
+    for (int c = 0; c < C; ++c) {
+        T s = T(0);
+        for (int64_t j = threadIdx.x; j < nrows; j += 256) s += grow[j * C + c];
+        sm[threadIdx.x] = s;
+        __syncthreads();
+        for (int h = 128; h > 0; h >>= 1) {
+            if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) opt_step(g, c, sm[0] * inv_bsz, o);
+        __syncthreads();
+    }
+}
+
+// ----------------------------------------------------------------- host --
+
+unsigned blocks_for(int64_t n, int nt) { return (unsigned)std::max<int64_t>(1, ceil_div(n, nt)); }
+
+int bits_for(int64_t n_keys) {
+    int b = 0;
+    while (b < 32 && ((int64_t)1 << b) < n_keys) ++b;
+    return b;
+}
+
+template <class T>
+struct Stream {
+    int kind = FEAT;
+    int64_t n_keys = 0;
+    int W = 0, cb1 = 0;
+    GroupDev<T> g0{}, g1{};
+    // per-epoch plan
+    DevBuf<int64_t> estart, seg_lo, run_start, item_start, item_run, long_list, bitem, blong;
+    DevBuf<uint32_t> k0, v0, k1, v1;
+    uint32_t *keys = nullptr, *vals = nullptr;
+    std::vector<int64_t> h_seg, h_item, h_long;
+    int64_t max_entries = 0, max_items = 0;
+    DevBuf<T> pay, part;
+};
+
+template <class T>
+struct Trainer {
+    int device;
+    cudaStream_t s;
+    Model model;
+    int C;
+    bool multiclass;
+    int64_t n_rows, n_feat, F, k, B, nb, E;
+    const mfm_train* tr;
+    // device data
+    DevBuf<int64_t> indptr;
+    DevBuf<int32_t> indices, order_all, fid, ycls;
+    DevBuf<T> data, y, sw, grow;
+    // parameters + state per group: 0 = w0, 1 = w, 2 = V, 3 = R
+    DevBuf<T> par[4], st[4][6];
+    GroupDev<T> G[4];
+    OptDev opt;
+    Stream<T> S[2];
+    int n_streams = 1;
+
+    void upload_group(int gi, const mfm_group* hg, int64_t R, int64_t K, int reg) {
+        const int64_t n = (int64_t)C * R * K;
+        auto up = [&](DevBuf<T>& dst, const double* src) {
+            dst.alloc(device, n);
+            if (!src) {
+                MFM_CUDA(cudaMemsetAsync(dst.ptr, 0, n * sizeof(T), s), "state init");
+                return;
+            }
+            DevBuf<double> tmp(device, n);
+            h2d(tmp.ptr, src, n, s, "parameter upload");
+            to_device_layout<T><<<blocks_for(n, 256), 256, 0, s>>>(tmp.ptr, dst.ptr, C, R, K);
+            MFM_CHECK_LAUNCH("layout");
+            MFM_CUDA(cudaStreamSynchronize(s), "parameter upload");
+        };
+        up(par[gi], hg->param);
+        GroupDev<T>& g = G[gi];
+        g = GroupDev<T>{par[gi].ptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                        (int64_t)C * K, reg};
+        const int kind = tr->optimizer;
+        if (kind == MFM_OPT_ADAGRAD) {
+            up(st[gi][0], hg->acc);
+            g.acc = st[gi][0].ptr;
+        } else if (kind == MFM_OPT_ADAM) {
+            up(st[gi][1], hg->m);
+            up(st[gi][2], hg->s);
+            up(st[gi][3], hg->t);
+            g.m = st[gi][1].ptr;
+            g.s = st[gi][2].ptr;
+            g.t = st[gi][3].ptr;
+        } else if (kind == MFM_OPT_FTRL) {
+            up(st[gi][4], hg->z);
+            up(st[gi][5], hg->n);
+            g.z = st[gi][4].ptr;
+            g.n = st[gi][5].ptr;
+        }
+    }
+
+    void download_group(int gi, mfm_group* hg, int64_t R, int64_t K) {
+        const int64_t n = (int64_t)C * R * K;
+        auto down = [&](DevBuf<T>& src, double* dst) {
+            if (!dst || !src.ptr) return;
+            DevBuf<double> tmp(device, n);
+            from_device_layout<T><<<blocks_for(n, 256), 256, 0, s>>>(src.ptr, tmp.ptr, C, R, K);
+            MFM_CHECK_LAUNCH("layout");
+            d2h(dst, tmp.ptr, n, s, "parameter download");
+            MFM_CUDA(cudaStreamSynchronize(s), "parameter download");
+        };
+        down(par[gi], hg->param);
+        const int kind = tr->optimizer;
+        if (kind == MFM_OPT_ADAGRAD) down(st[gi][0], hg->acc);
+        if (kind == MFM_OPT_ADAM) {
+            down(st[gi][1], hg->m);
+            down(st[gi][2], hg->s);
+            down(st[gi][3], hg->t);
+        }
+        if (kind == MFM_OPT_FTRL) {
+            down(st[gi][4], hg->z);
+            down(st[gi][5], hg->n);
+        }
+    }
+
+    // count -> scan -> expand -> segmented sort -> runs -> items, for epoch e
+    void plan(Stream<T>& st_, int e) {
+        const int32_t* order = order_all.ptr + (int64_t)e * n_rows;
+        DevBuf<int64_t> cnt(device, n_rows);
+        st_.estart.alloc(device, n_rows + 1);
+        count_kernel<<<blocks_for(n_rows, 256), 256, 0, s>>>(st_.kind, order, indptr.ptr, n_rows,
+                                                           cnt.ptr);
+        exclusive_scan<int64_t, int64_t>(device, s, cnt.ptr, n_rows, st_.estart.ptr);
+        st_.seg_lo.alloc(device, nb + 1);
+        seg_lo_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(st_.estart.ptr, n_rows, B, nb,
+                                                            st_.seg_lo.ptr);
+        st_.h_seg.resize(nb + 1);
+        d2h(st_.h_seg.data(), st_.seg_lo.ptr, nb + 1, s, "plan download");
+        MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        const int64_t N = st_.h_seg[nb];
+        st_.max_entries = 0;
+        for (int64_t b = 0; b < nb; ++b) {
+            const int64_t len = st_.h_seg[b + 1] - st_.h_seg[b];
+            if (len >= ((int64_t)1 << 32))
+                fail(MFM_ERR_UNSUPPORTED, "a batch has 2^32 or more gradient entries");
+            st_.max_entries = std::max(st_.max_entries, len);
+        }
+        if (st_.k0.n < (size_t)N || !st_.k0.ptr) {
+            st_.k0.alloc(device, N);
+            st_.v0.alloc(device, N);
+            st_.k1.alloc(device, N);
+            st_.v1.alloc(device, N);
+        }
+        expand_kernel<<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
+            st_.kind, order, indptr.ptr, indices.ptr, fid.ptr, (int)F, n_rows, B,
+            st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr);
+        MFM_CHECK_LAUNCH("expand");
+        SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr,
+                                       st_.seg_lo.ptr, nb, N, bits_for(st_.n_keys));
+        st_.keys = sr.keys;
+        st_.vals = sr.vals;
+        DevBuf<int32_t> head(device, N);
+        DevBuf<int64_t> run_id(device, N + 1);
+        if (N > 0) {
+            head_kernel<<<blocks_for(N, 256), 256, 0, s>>>(st_.keys, N, head.ptr);
+            seg_head_kernel<<<blocks_for(nb, 256), 256, 0, s>>>(st_.seg_lo.ptr, nb, head.ptr);
+        }
+        exclusive_scan<int32_t, int64_t>(device, s, head.ptr, N, run_id.ptr);
+        int64_t Rn = 0;
+        d2h(&Rn, run_id.ptr + N, 1, s, "plan download");
+        MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        st_.run_start.alloc(device, Rn + 1);
+        run_start_kernel<<<blocks_for(std::max<int64_t>(N, 1), 256), 256, 0, s>>>(
+            head.ptr, run_id.ptr, N, st_.run_start.ptr);
+        DevBuf<int64_t> np(device, Rn), lf(device, Rn), lscan(device, Rn + 1);
+        st_.item_start.alloc(device, Rn + 1);
+        if (Rn > 0)
+            pieces_kernel<<<blocks_for(Rn, 256), 256, 0, s>>>(st_.run_start.ptr, Rn, np.ptr,
+                                                            lf.ptr);
+        exclusive_scan<int64_t, int64_t>(device, s, np.ptr, Rn, st_.item_start.ptr);
+        exclusive_scan<int64_t, int64_t>(device, s, lf.ptr, Rn, lscan.ptr);
+        int64_t tot[2] = {0, 0};
+        d2h(&tot[0], st_.item_start.ptr + Rn, 1, s, "plan download");
+        d2h(&tot[1], lscan.ptr + Rn, 1, s, "plan download");
+        MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        st_.item_run.alloc(device, tot[0]);
+        st_.long_list.alloc(device, tot[1]);
+        if (Rn > 0)
+            items_kernel<<<blocks_for(Rn, 256), 256, 0, s>>>(st_.item_start.ptr, lscan.ptr, Rn,
+                                                           st_.item_run.ptr, st_.long_list.ptr);
+        st_.bitem.alloc(device, nb + 1);
+        st_.blong.alloc(device, nb + 1);
+        batch_tables_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(
+            st_.seg_lo.ptr, nb, run_id.ptr, st_.item_start.ptr, lscan.ptr, st_.bitem.ptr,
+            st_.blong.ptr);
+        MFM_CHECK_LAUNCH("plan");
+        st_.h_item.resize(nb + 1);
+        st_.h_long.resize(nb + 1);
+        d2h(st_.h_item.data(), st_.bitem.ptr, nb + 1, s, "plan download");
+        d2h(st_.h_long.data(), st_.blong.ptr, nb + 1, s, "plan download");
+        MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        st_.max_items = 0;
+        for (int64_t b = 0; b < nb; ++b)
+            st_.max_items = std::max(st_.max_items, st_.h_item[b + 1] - st_.h_item[b]);
+        if (st_.pay.n < (size_t)(st_.max_entries * st_.W) || !st_.pay.ptr)
+            st_.pay.alloc(device, std::max<int64_t>(1, st_.max_entries * st_.W));
+        if (st_.part.n < (size_t)(st_.max_items * st_.W) || !st_.part.ptr)
+            st_.part.alloc(device, std::max<int64_t>(1, st_.max_items * st_.W));
+    }
+
+    RedArgs<T> red_args(Stream<T>& st_, T inv_bsz) {
+        RedArgs<T> R;
+        R.keys = st_.keys;
+        R.vals = st_.vals;
+        R.run_start = st_.run_start.ptr;
+        R.item_start = st_.item_start.ptr;
+        R.item_run = st_.item_run.ptr;
+        R.long_list = st_.long_list.ptr;
+        R.pay = st_.pay.ptr;
+        R.part = st_.part.ptr;
+        R.W = st_.W;
+        R.cb1 = st_.cb1;
+        R.g0 = st_.g0;
+        R.g1 = st_.g1;
+        R.opt = opt;
+        R.inv_bsz = inv_bsz;
+        return R;
+    }
+
+    void launch_forward(const FwdArgs<T>& A, int64_t nrows) {
+        const unsigned grid = warp_grid(device, nrows, 8, 8);
+        if (model == M_FM) {
+            const int D = C * (int)k;
+            int Lc = 1, lgc = 0;
+            while (Lc < D && Lc < 32) {
+                Lc <<= 1;
+                ++lgc;
+            }
+            const int mcol = (D + Lc - 1) / Lc;
+            const size_t sm = (size_t)8 * (D + 3 * C) * sizeof(T);
+#define MFM_FWD(MC)                                                                   \
+    if (mcol <= MC) {                                                                 \
+        if (sm > 48 * 1024)                                                           \
+            MFM_CUDA(cudaFuncSetAttribute(fm_forward_kernel<T, MC>,                   \
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                          (int)sm),                                   \
+                     "forward smem attribute");                                       \
+        fm_forward_kernel<T, MC><<<grid, 256, sm, s>>>(A, lgc);                       \
+        MFM_CHECK_LAUNCH("FM forward");                                               \
+        return;                                                                       \
+    }
+            MFM_FWD(1)
+            MFM_FWD(2)
+            MFM_FWD(4)
+            MFM_FWD(8)
+            MFM_FWD(16)
+            MFM_FWD(32)
+#undef MFM_FWD
+            fail(MFM_ERR_UNSUPPORTED, "n_classes * k exceeds 1024");
+        }
+        const size_t sm = (size_t)8 * 2 * C * sizeof(T);
+        constexpr int maxv = 16 / sizeof(T);
+        const bool v4 = k % maxv == 0, v2 = k % 2 == 0;
+        if (model == M_FFM) {
+            if (v4)
+                ffm_forward_kernel<T, maxv><<<grid, 256, sm, s>>>(A);
+            else if (v2)
+                ffm_forward_kernel<T, 2><<<grid, 256, sm, s>>>(A);
+            else
+                ffm_forward_kernel<T, 1><<<grid, 256, sm, s>>>(A);
+        } else {
+            if (v4)
+                fwfm_forward_kernel<T, maxv><<<grid, 256, sm, s>>>(A);
+            else if (v2)
+                fwfm_forward_kernel<T, 2><<<grid, 256, sm, s>>>(A);
+            else
+                fwfm_forward_kernel<T, 1><<<grid, 256, sm, s>>>(A);
+        }
+        MFM_CHECK_LAUNCH("forward");
+    }
+
+    void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz) {
+        const int64_t i0 = st_.h_item[b], i1 = st_.h_item[b + 1];
+        const int64_t l0 = st_.h_long[b], l1 = st_.h_long[b + 1];
+        RedArgs<T> R = red_args(st_, inv_bsz);
+        if (i1 > i0) {
+            const unsigned grid = blocks_for(i1 - i0, 8);
+            if (st_.W <= 32)
+                reduce_stage1_kernel<T, 1><<<grid, 256, 0, s>>>(R, i0, i1);
+            else if (st_.W <= 64)
+                reduce_stage1_kernel<T, 2><<<grid, 256, 0, s>>>(R, i0, i1);
+            else
+                reduce_stage1_kernel<T, 4><<<grid, 256, 0, s>>>(R, i0, i1);
+            MFM_CHECK_LAUNCH("reduce stage 1");
+        }
+        if (l1 > l0) {
+            reduce_stage2_kernel<T><<<blocks_for(l1 - l0, 8), 256, 0, s>>>(R, l0, l1, i0);
+            MFM_CHECK_LAUNCH("reduce stage 2");
+        }
+    }
+
+    void run(const FwdArgs<T>& base) {
+        for (int64_t e = 0; e < E; ++e) {
+            for (int si = 0; si < n_streams; ++si) plan(S[si], (int)e);
+            for (int64_t b = 0; b < nb; ++b) {
+                const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
+                const T inv_bsz = T(1) / (T)nrows;  // divide by batch length (fm.rs:395-398)
+                FwdArgs<T> A = base;
+                A.order = order_all.ptr + e * n_rows;
+                A.pos0 = pos0;
+                A.nrows = nrows;
+                A.estart1 = S[0].estart.ptr;
+                A.seg1 = S[0].h_seg[b];
+                A.pay1 = S[0].pay.ptr;
+                A.W1 = S[0].W;
+                if (n_streams > 1) {
+                    A.estart2 = S[1].estart.ptr;
+                    A.seg2 = S[1].h_seg[b];
+                    A.pay2 = S[1].pay.ptr;
+                    A.W2 = S[1].W;
+                }
+                launch_forward(A, nrows);
+                for (int si = 0; si < n_streams; ++si) launch_reduce(S[si], b, inv_bsz);
+                w0_kernel<T><<<1, 256, 0, s>>>(grow.ptr, nrows, C, G[0], opt, inv_bsz);
+                MFM_CHECK_LAUNCH("w0 step");
+            }
+        }
+        MFM_CUDA(cudaStreamSynchronize(s), "training");
+    }
+};
+
+// ------------------------------------------------------------- entry point --
+
+struct FitSpec {
+    Model model;
+    bool multiclass;
+    int64_t C;
+    const mfm_csr* x;
+    const double* y;
+    const int64_t* ycls;
+    const double* sw;
+    const int64_t* field_ids;
+    int64_t F;
+    const mfm_train* tr;
+    int64_t k;
+    mfm_group *w0, *w, *v, *r;
+};
+
+void validate_fit(const FitSpec& f) {
+    check_csr_host(f.x);
+    const mfm_train* tr = f.tr;
+    if (!tr) fail(MFM_ERR_INVALID, "missing training configuration");
+    if (tr->batch_size < 1) fail(MFM_ERR_INVALID, "batch_size must be >= 1");
+    if (tr->optimizer < MFM_OPT_SGD || tr->optimizer > MFM_OPT_FTRL)
+        fail(MFM_ERR_INVALID, fmt("unknown optimizer %d", tr->optimizer));
+    if (!f.multiclass && tr->loss != MFM_LOSS_LOGISTIC && tr->loss != MFM_LOSS_SQUARED)
+        fail(MFM_ERR_INVALID, fmt("unknown loss %d", tr->loss));
+    if (f.k < 1 || f.k > 1024)
+        fail(MFM_ERR_UNSUPPORTED,
+             fmt("CUDA training supports 1 <= k <= 1024, got %lld", (long long)f.k));
+    if (f.C < 1) fail(MFM_ERR_INVALID, "n_classes must be >= 1");
+    if (f.multiclass && f.C > 32)
+        fail(MFM_ERR_UNSUPPORTED,
+             fmt("CUDA multiclass training supports up to 32 classes, got %lld", (long long)f.C));
+    if (f.model == M_FM && f.C * f.k > 1024)
+        fail(MFM_ERR_UNSUPPORTED, "n_classes * k must be <= 1024");
+    if (f.model != M_FM) check_field_ids(f.field_ids, f.x->n_features, f.F);
+    if (f.model == M_FFM && f.x->n_features * f.F >= ((int64_t)1 << 32))
+        fail(MFM_ERR_UNSUPPORTED, "n_features * n_fields must be < 2^32");
+    const int64_t n = f.x->n_rows;
+    if (n >= ((int64_t)1 << 31)) fail(MFM_ERR_UNSUPPORTED, "n_rows must be < 2^31");
+    if (tr->n_epochs < 0 || (tr->n_epochs > 0 && !tr->row_orders))
+        fail(MFM_ERR_INVALID, "row_orders must be (n_epochs, n_rows)");
+    for (int64_t i = 0; i < tr->n_epochs * n; ++i)
+        if (tr->row_orders[i] < 0 || tr->row_orders[i] >= n)
+            fail(MFM_ERR_INVALID, fmt("row_orders entry out of range [0, %lld)", (long long)n));
+    if (f.multiclass)
+        for (int64_t i = 0; i < n; ++i)
+            if (f.ycls[i] < 0 || f.ycls[i] >= f.C)
+                fail(MFM_ERR_INVALID,
+                     fmt("class index out of range [0, %lld)", (long long)f.C));
+    if (!f.w0 || !f.w || !f.v || !f.w0->param || !f.w->param || !f.v->param ||
+        (f.model == M_FWFM && (!f.r || !f.r->param)))
+        fail(MFM_ERR_INVALID, "parameter arrays must be provided");
+}
+
+template <class T>
+void fit_impl(const FitSpec& f, int device) {
+    DeviceGuard guard(device);
+    std::lock_guard<std::mutex> lk(device_mutex(device));
+    Trainer<T> tr;
+    tr.device = device;
+    tr.s = device_stream(device);
+    cudaStream_t s = tr.s;
+    tr.model = f.model;
+    tr.C = (int)f.C;
+    tr.multiclass = f.multiclass;
+    tr.n_rows = f.x->n_rows;
+    tr.n_feat = f.x->n_features;
+    tr.F = f.model == M_FM ? 1 : f.F;
+    tr.k = f.k;
+    tr.B = f.tr->batch_size;
+    tr.E = f.tr->n_epochs;
+    tr.tr = f.tr;
+    tr.nb = tr.n_rows > 0 ? ceil_div(tr.n_rows, tr.B) : 0;
+    const int64_t n = tr.n_rows, nnz = f.x->nnz, nf = tr.n_feat;
+
+    // data upload (indices narrowed to int32 and values to T on the device)
+    tr.indptr.alloc(device, n + 1);
+    h2d(tr.indptr.ptr, f.x->indptr, n + 1, s, "indptr upload");
+    {
+        DevBuf<int64_t> ix64(device, nnz);
+        h2d(ix64.ptr, f.x->indices, nnz, s, "indices upload");
+        validate_csr_device(device, s, tr.indptr.ptr, n, ix64.ptr, nnz, nf);
+        tr.indices.alloc(device, nnz);
+        convert_kernel<int64_t, int32_t><<<blocks_for(nnz, 256), 256, 0, s>>>(ix64.ptr,
+                                                                            tr.indices.ptr, nnz);
+        DevBuf<double> d64(device, nnz);
+        h2d(d64.ptr, f.x->data, nnz, s, "data upload");
+        tr.data.alloc(device, nnz);
+        convert_kernel<double, T><<<blocks_for(nnz, 256), 256, 0, s>>>(d64.ptr, tr.data.ptr, nnz);
+        DevBuf<double> sw64(device, n);
+        h2d(sw64.ptr, f.sw, n, s, "sample_weight upload");
+        tr.sw.alloc(device, n);
+        convert_kernel<double, T><<<blocks_for(n, 256), 256, 0, s>>>(sw64.ptr, tr.sw.ptr, n);
+        if (f.multiclass) {
+            DevBuf<int64_t> y64(device, n);
+            h2d(y64.ptr, f.ycls, n, s, "y upload");
+            tr.ycls.alloc(device, n);
+            convert_kernel<int64_t, int32_t><<<blocks_for(n, 256), 256, 0, s>>>(y64.ptr,
+                                                                              tr.ycls.ptr, n);
+        } else {
+            DevBuf<double> y64(device, n);
+            h2d(y64.ptr, f.y, n, s, "y upload");
+            tr.y.alloc(device, n);
+            convert_kernel<double, T><<<blocks_for(n, 256), 256, 0, s>>>(y64.ptr, tr.y.ptr, n);
+        }
+        const int64_t nro = tr.E * n;
+        DevBuf<int64_t> ro64(device, nro);
+        h2d(ro64.ptr, f.tr->row_orders, nro, s, "row_orders upload");
+        tr.order_all.alloc(device, nro);
+        convert_kernel<int64_t, int32_t><<<blocks_for(nro, 256), 256, 0, s>>>(
+            ro64.ptr, tr.order_all.ptr, nro);
+        MFM_CHECK_LAUNCH("upload conversion");
+        MFM_CUDA(cudaStreamSynchronize(s), "upload");
+    }
+    if (f.model != M_FM) {
+        std::vector<int32_t> f32(nf);
+        for (int64_t i = 0; i < nf; ++i) f32[i] = (int32_t)f.field_ids[i];
+        tr.fid.alloc(device, nf);
+        h2d(tr.fid.ptr, f32.data(), nf, s, "field_ids upload");
+        MFM_CUDA(cudaStreamSynchronize(s), "field_ids upload");
+    }
+
+    // parameters + optimizer state, device layout (key, class, k)
+    const int64_t F = tr.F, k = tr.k;
+    tr.upload_group(0, f.w0, 1, 1, 2);
+    tr.upload_group(1, f.w, nf, 1, 0);
+    if (f.model == M_FFM)
+        tr.upload_group(2, f.v, nf * F, k, 1);
+    else
+        tr.upload_group(2, f.v, nf, k, 1);
+    if (f.model == M_FWFM) tr.upload_group(3, f.r, F * F, 1, 1);
+
+    const mfm_train* c = f.tr;
+    tr.opt = OptDev{c->optimizer, c->learning_rate, c->beta_1, c->beta_2, c->epsilon,
+                    c->ftrl_beta, {c->l1_linear, c->l1_factors, 0.0},
+                    {c->l2_linear, c->l2_factors, 0.0}};
+
+    // entry streams
+    const int C = tr.C;
+    Stream<T>& s0 = tr.S[0];
+    s0.kind = FEAT;
+    s0.n_keys = nf;
+    s0.g0 = tr.G[1];
+    if (f.model == M_FFM) {
+        s0.W = C;
+        s0.cb1 = C;
+        s0.g1 = tr.G[1];
+        Stream<T>& s1 = tr.S[1];
+        s1.kind = SLOT;
+        s1.n_keys = nf * F;
+        s1.W = (int)(C * k);
+        s1.cb1 = s1.W;
+        s1.g0 = tr.G[2];
+        s1.g1 = tr.G[2];
+        tr.n_streams = 2;
+    } else {
+        s0.W = (int)(C + C * k);
+        s0.cb1 = C;
+        s0.g1 = tr.G[2];
+        if (f.model == M_FWFM) {
+            Stream<T>& s1 = tr.S[1];
+            s1.kind = PAIR;
+            s1.n_keys = F * F;
+            s1.W = C;
+            s1.cb1 = C;
+            s1.g0 = tr.G[3];
+            s1.g1 = tr.G[3];
+            tr.n_streams = 2;
+        }
+    }
+    tr.grow.alloc(device, std::max<int64_t>(1, std::min(tr.B, n)) * C);
+
+    FwdArgs<T> A{};
+    A.indptr = tr.indptr.ptr;
+    A.indices = tr.indices.ptr;
+    A.data = tr.data.ptr;
+    A.y = tr.y.ptr;
+    A.ycls = tr.ycls.ptr;
+    A.sw = tr.sw.ptr;
+    A.C = C;
+    A.k = (int)k;
+    A.F = (int)F;
+    A.loss = c->loss;
+    A.multiclass = f.multiclass ? 1 : 0;
+    A.ls_on = (T)(1.0 - c->label_smoothing);
+    A.ls_off = (T)(C > 1 ? c->label_smoothing / ((double)C - 1.0) : 0.0);
+    A.w0 = tr.par[0].ptr;
+    A.w = tr.par[1].ptr;
+    A.v = tr.par[2].ptr;
+    A.r = tr.par[3].ptr;
+    A.fid = tr.fid.ptr;
+    A.grow = tr.grow.ptr;
+    if (n > 0) tr.run(A);
+
+    tr.download_group(0, f.w0, 1, 1);
+    tr.download_group(1, f.w, nf, 1);
+    if (f.model == M_FFM)
+        tr.download_group(2, f.v, nf * F, k);
+    else
+        tr.download_group(2, f.v, nf, k);
+    if (f.model == M_FWFM) tr.download_group(3, f.r, F * F, 1);
+}
+
+void fit_dispatch(const FitSpec& f, const mfm_exec* ex) {
+    validate_fit(f);
+    const int dtype = ex ? ex->dtype : MFM_DTYPE_F64;
+    const int device = ex ? ex->device : 0;
+    if (dtype == MFM_DTYPE_F64)
+        fit_impl<double>(f, device);
+    else if (dtype == MFM_DTYPE_F32)
+        fit_impl<float>(f, device);
+    else
+        fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
+}
+
+}  // namespace mfm
+
+using namespace mfm;
+
+extern "C" int mfm_fm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                              const mfm_train* tr, int64_t k, mfm_group* w0, mfm_group* w,
+                              mfm_group* v, const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FM, false, 1, x, y, nullptr, sample_weight, nullptr, 0, tr, k, w0, w, v,
+                  nullptr};
+        fit_dispatch(f, ex);
+    });
+}
+
+extern "C" int mfm_fm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                                         const double* sample_weight, int64_t n_classes,
+                                         const mfm_train* tr, int64_t k, mfm_group* w0,
+                                         mfm_group* w, mfm_group* v, const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FM, true, n_classes, x, nullptr, y, sample_weight, nullptr, 0, tr, k,
+                  w0, w, v, nullptr};
+        fit_dispatch(f, ex);
+    });
+}
+
+extern "C" int mfm_ffm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                               const int64_t* field_ids, int64_t n_fields, const mfm_train* tr,
+                               int64_t k, mfm_group* w0, mfm_group* w, mfm_group* v,
+                               const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FFM, false, 1, x, y, nullptr, sample_weight, field_ids, n_fields, tr, k,
+                  w0, w, v, nullptr};
+        fit_dispatch(f, ex);
+    });
+}
+
+extern "C" int mfm_ffm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                                          const double* sample_weight, int64_t n_classes,
+                                          const int64_t* field_ids, int64_t n_fields,
+                                          const mfm_train* tr, int64_t k, mfm_group* w0,
+                                          mfm_group* w, mfm_group* v, const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FFM, true, n_classes, x, nullptr, y, sample_weight, field_ids, n_fields,
+                  tr, k, w0, w, v, nullptr};
+        fit_dispatch(f, ex);
+    });
+}
+
+extern "C" int mfm_fwfm_fit_csr(const mfm_csr* x, const double* y, const double* sample_weight,
+                                const int64_t* field_ids, int64_t n_fields, const mfm_train* tr,
+                                int64_t k, mfm_group* w0, mfm_group* w, mfm_group* v,
+                                mfm_group* r, const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FWFM, false, 1, x, y, nullptr, sample_weight, field_ids, n_fields, tr, k,
+                  w0, w, v, r};
+        fit_dispatch(f, ex);
+    });
+}
+
+extern "C" int mfm_fwfm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
+                                           const double* sample_weight, int64_t n_classes,
+                                           const int64_t* field_ids, int64_t n_fields,
+                                           const mfm_train* tr, int64_t k, mfm_group* w0,
+                                           mfm_group* w, mfm_group* v, mfm_group* r,
+                                           const mfm_exec* ex) {
+    return guarded([&] {
+        FitSpec f{M_FWFM, true, n_classes, x, nullptr, y, sample_weight, field_ids, n_fields,
+                  tr, k, w0, w, v, r};
+        fit_dispatch(f, ex);
+    });
+}

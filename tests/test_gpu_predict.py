@@ -1,0 +1,181 @@
+"""GPU parity of the CSR scoring kernels (FM / FFM / FwFM), through the C ABI,
+against the C oracle and the reference's NumPy golden outputs.
+
+Tolerances: float64 compute uses the reference's own CUDA bar, rtol = atol =
+1e-10 (tests/test_cuda_parity.py:30-31); float32 compute uses the target bar
+of 1e-5 relative, with an absolute floor of 1e-5 times the row's magnitude
+scale (sum of |terms|) so that scores near zero are judged on their scale.
+"""
+
+import numpy as np
+import pytest
+import scipy.sparse as sp
+
+import golden_io
+import run_cases
+from modern_fm_b200 import _rust
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+RTOL64 = ATOL64 = 1e-10
+RTOL32 = 1e-5
+
+
+@pytest.fixture
+def f32(monkeypatch):
+    monkeypatch.setenv("MFM_B200_DTYPE", "float32")
+
+
+def _scale_fm(ip, ix, dv, w0, w, V):
+    """Per-row sum of the absolute terms of the FM score (for float32 atol)."""
+    n = len(ip) - 1
+    X = sp.csr_matrix((np.abs(dv), ix, ip), shape=(n, len(w)))
+    aV = np.abs(V)
+    return abs(w0) + X @ np.abs(w) + 0.5 * ((X @ aV) ** 2).sum(axis=1) + 1.0
+
+
+def _random_csr(rng, n, d, density):
+    X = rng.normal(size=(n, d))
+    X[rng.random(size=X.shape) > density] = 0.0
+    Xc = sp.csr_matrix(X)
+    return Xc.indptr.astype(np.int64), Xc.indices.astype(np.int64), Xc.data
+
+
+@pytest.mark.parametrize("case", golden_io.load("predict.npz"), ids=lambda c: c.name)
+def test_predict_golden_f64(case):
+    got = run_cases.predict_case(_rust, case, cuda=True)
+    np.testing.assert_allclose(got, case.a["out"], rtol=RTOL64, atol=ATOL64)
+    np.testing.assert_allclose(got, run_cases.predict_case(O, case, cuda=False), rtol=RTOL64,
+                               atol=ATOL64)
+
+
+@pytest.mark.parametrize("case", golden_io.load("predict.npz"), ids=lambda c: c.name)
+def test_predict_golden_f32(case, f32):
+    got = run_cases.predict_case(_rust, case, cuda=True)
+    want = case.a["out"]
+    a = case.a
+    if case["model"] == "fm":
+        scale = _scale_fm(a["indptr"], a["indices"], a["data"], case["w0"], a["w"], a["V"])
+    else:
+        scale = np.abs(want) + 10.0 * np.abs(a["V"]).max() ** 2 * 50
+    assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-5 * scale)
+
+
+@pytest.mark.parametrize("k", [1, 3, 4, 16, 17, 64, 130, 1024])
+def test_fm_predict_k_range(k):
+    rng = np.random.default_rng(k)
+    ip, ix, dv = _random_csr(rng, 300, 60, 0.2)
+    w0, w, V = rng.normal(), rng.normal(size=60), rng.normal(size=(60, k))
+    want = O.fm_predict_fast_csr(ip, ix, dv, 60, w0, w, V)
+    got = _rust.fm_predict_cuda_csr(ip, ix, dv, 60, w0, w, V)
+    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=1e-9 * max(1.0, k / 16))
+
+
+def test_empty_rows_and_single_nonzero():
+    # tests/test_cuda_parity.py:51-64
+    X = sp.csr_matrix((4, 6))
+    out = _rust.fm_predict_cuda_csr(X.indptr, X.indices, X.data, 6, 1.5, np.zeros(6),
+                                    np.ones((6, 3)))
+    np.testing.assert_allclose(out, np.full(4, 1.5), rtol=RTOL64, atol=ATOL64)
+    Xd = np.zeros((3, 5))
+    Xd[1, 2] = -2.0
+    Xc = sp.csr_matrix(Xd)
+    w = np.arange(5.0)
+    out = _rust.fm_predict_cuda_csr(Xc.indptr, Xc.indices, Xc.data, 5, 0.5, w,
+                                    np.ones((5, 4)))
+    np.testing.assert_allclose(out, [0.5, 0.5 + w[2] * -2.0, 0.5], rtol=RTOL64, atol=ATOL64)
+    fid = np.array([0, 1, 2, 0, 1])
+    out = _rust.ffm_predict_cuda_csr(Xc.indptr, Xc.indices, Xc.data, 5, fid, 0.5, w,
+                                     np.ones((5, 3, 4)))
+    np.testing.assert_allclose(out, [0.5, 0.5 + w[2] * -2.0, 0.5], rtol=RTOL64, atol=ATOL64)
+    out = _rust.fwfm_predict_cuda_csr(Xc.indptr, Xc.indices, Xc.data, 5, fid, 0.5, w,
+                                      np.ones((5, 4)), np.ones((3, 3)))
+    np.testing.assert_allclose(out, [0.5, 0.5 + w[2] * -2.0, 0.5], rtol=RTOL64, atol=ATOL64)
+
+
+def test_zero_row_matrix():
+    out = _rust.fm_predict_cuda_csr(np.array([0]), np.array([], dtype=np.int64), np.array([]),
+                                    3, 1.0, np.zeros(3), np.zeros((3, 2)))
+    assert out.shape == (0,)
+
+
+def test_known_answers():
+    # FM 4.25 (rust/src/fm.rs:433-441), FFM 9.5 (ffm.rs:454-474), FwFM 10.25 (fwfm.rs:411-420)
+    ip, ix, dv = np.array([0, 2]), np.array([0, 1]), np.array([2.0, 3.0])
+    V = np.array([[1.0, 0.0], [1.0, 1.0]])
+    out = _rust.fm_predict_cuda_csr(ip, ix, dv, 2, 0.25, np.array([0.5, -1.0]), V)
+    assert abs(out[0] - 4.25) < 1e-12
+    r = np.ones((2, 2))
+    r[0, 1] = 2.0
+    out = _rust.fwfm_predict_cuda_csr(ip, ix, dv, 2, np.array([0, 1]), 0.25,
+                                      np.array([0.5, -1.0]), V, r)
+    assert abs(out[0] - 10.25) < 1e-12
+    V3 = np.zeros((3, 2, 2))
+    V3[0, 0], V3[0, 1] = [1.0, 0.0], [0.0, 1.0]
+    V3[1, 0], V3[1, 1] = [1.0, 1.0], [2.0, 0.0]
+    V3[2, 0], V3[2, 1] = [0.5, 0.5], [1.0, -1.0]
+    out = _rust.ffm_predict_cuda_csr(np.array([0, 3]), np.array([0, 1, 2]),
+                                     np.array([1.0, 2.0, 3.0]), 3, np.array([0, 0, 1]), 0.0,
+                                     np.zeros(3), V3)
+    assert abs(out[0] - 9.5) < 1e-12
+
+
+def test_ffm_large_row():
+    # a single row with z = 2048 nonzeros (tests/test_cuda_parity.py:126-136)
+    rng = np.random.default_rng(0)
+    d = 2048
+    X = sp.csr_matrix(rng.normal(size=(1, d)))
+    w0, w = float(rng.normal()), rng.normal(size=d)
+    V = rng.normal(size=(d, 4, 4))
+    fid = rng.integers(0, 4, size=d)
+    want = O.ffm_predict_csr(X.indptr, X.indices, X.data, d, fid, w0, w, V)
+    got = _rust.ffm_predict_cuda_csr(X.indptr, X.indices, X.data, d, fid, w0, w, V)
+    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=ATOL64)
+    Vf = rng.normal(size=(d, 4))
+    r = rng.uniform(size=(4, 4))
+    want = O.fwfm_predict_csr(X.indptr, X.indices, X.data, d, fid, w0, w, Vf, r)
+    got = _rust.fwfm_predict_cuda_csr(X.indptr, X.indices, X.data, d, fid, w0, w, Vf, r)
+    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=1e-9)
+
+
+def test_predict_validation_on_device():
+    ip, ix, dv = np.array([0, 1, 2]), np.array([0, 5]), np.ones(2)
+    with pytest.raises(ValueError, match=r"column index out of range \[0, 3\)"):
+        _rust.fm_predict_cuda_csr(ip, ix, dv, 3, 0.0, np.zeros(3), np.zeros((3, 2)))
+    with pytest.raises(ValueError, match="indptr must be non-decreasing"):
+        _rust.fm_predict_cuda_csr(np.array([0, 2, 1, 2]), np.array([0, 1]), np.ones(2), 3, 0.0,
+                                  np.zeros(3), np.zeros((3, 2)))
+    with pytest.raises(ValueError, match=r"field id out of range \[0, 2\)"):
+        _rust.ffm_predict_cuda_csr(np.array([0, 1]), np.array([0]), np.ones(1), 2,
+                                   np.array([0, 2]), 0.0, np.zeros(2), np.zeros((2, 2, 2)))
+    with pytest.raises(RuntimeError, match="1 <= k <= 1024"):
+        _rust.fm_predict_cuda_csr(np.array([0, 1]), np.array([0]), np.ones(1), 2, 0.0,
+                                  np.zeros(2), np.zeros((2, 1025)))
+
+
+def test_ctr_shaped_f32_against_oracle(f32):
+    """A CTR-shaped FM workload (39 fields, Zipf ids, k=16) in float32."""
+    from modern_fm_b200 import workloads
+
+    X, _ = workloads.ctr_fm(n_rows=20000, seed=5)
+    rng = np.random.default_rng(1)
+    d = X.n_features
+    w0, w, V = -3.0, rng.normal(0, 0.1, d), rng.normal(0, 0.1, (d, 16))
+    want = O.fm_predict_fast_csr(X.indptr, X.indices, X.data, d, w0, w, V, n_threads=4)
+    got = _rust.fm_predict_cuda_csr(X.indptr, X.indices, X.data, d, w0, w, V)
+    scale = _scale_fm(X.indptr, X.indices, X.data, w0, w, V)
+    assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-6 * scale)
+
+
+def test_multi_device_sharding_matches_single(monkeypatch):
+    if _rust.has_cuda() and __import__("modern_fm_b200._lib", fromlist=["x"]).lib(
+    ).mfm_device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    rng = np.random.default_rng(3)
+    ip, ix, dv = _random_csr(rng, 5000, 100, 0.1)
+    w0, w, V = rng.normal(), rng.normal(size=100), rng.normal(size=(100, 8))
+    one = _rust.fm_predict_cuda_csr(ip, ix, dv, 100, w0, w, V)
+    monkeypatch.setenv("MFM_B200_NUM_GPUS", "2")
+    two = _rust.fm_predict_cuda_csr(ip, ix, dv, 100, w0, w, V)
+    np.testing.assert_array_equal(one, two)
