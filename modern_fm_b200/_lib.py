@@ -115,15 +115,17 @@ def ptr(a, kind=f64p):
     return None if a is None else a.ctypes.data_as(kind)
 
 
-def make_csr(indptr, indices, data, n_features):
-    """(Csr struct, keepalive) for int64/float64 C-contiguous CSR arrays."""
+def make_csr(indptr, indices, data, n_features, exc=ValueError):
+    """(Csr struct, keepalive) for int64/float64 C-contiguous CSR arrays.
+    `exc` is the exception type for a malformed CSR (the reference raises
+    RuntimeError from predict and ValueError from fit)."""
     indptr = np.ascontiguousarray(indptr, dtype=np.int64)
     indices = np.ascontiguousarray(indices, dtype=np.int64)
     data = np.ascontiguousarray(data, dtype=np.float64)
     if indptr.size == 0:
-        raise ValueError("indptr must have length n_rows + 1 (>= 1)")
+        raise exc("indptr must have length n_rows + 1 (>= 1)")
     if indices.size != data.size:
-        raise ValueError(
+        raise exc(
             f"indices and data length mismatch: {indices.size} vs {data.size}")
     c = Csr(ptr(indptr, i64p), ptr(indices, i64p), ptr(data), indptr.size - 1, data.size,
             int(n_features))

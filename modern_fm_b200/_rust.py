@@ -38,10 +38,23 @@ def has_cuda() -> bool:
 
 
 def _raise(rc, fit):
+    """Error types of the reference boundary: every error raised inside a CUDA
+    predict call (CSR structure, k range, device) is a RuntimeError
+    (rust/src/lib.rs:1506-1512); every fit error is a ValueError (lib.rs:437).
+    Shape and field-id checks run before the call and raise ValueError."""
     msg = L.last_error()
-    if rc < 0 or fit:  # fit errors are ValueError in the reference (lib.rs:437)
+    if fit:
         raise ValueError(msg)
     raise RuntimeError(msg)
+
+
+def _check_field_ids(field_ids, n_features, n_fields):
+    # check_field_ids, rust/src/data.rs:71-83 (ValueError, before the device call)
+    if field_ids.size != n_features:
+        raise ValueError(
+            f"field_ids length {field_ids.size} does not match n_features {n_features}")
+    if field_ids.size and (field_ids.min() < 0 or field_ids.max() >= n_fields):
+        raise ValueError(f"field id out of range [0, {n_fields})")
 
 
 def _f64(a):
@@ -75,7 +88,7 @@ def fm_predict_cuda_csr(indptr, indices, data, n_features, w0, w, v):
     if v.ndim != 2:
         raise ValueError(f"V must be 2-D (n_features, k), got shape {v.shape}")
     _check_w_v(n_features, w, v.shape[0])
-    csr, keep = L.make_csr(indptr, indices, data, n_features)
+    csr, keep = L.make_csr(indptr, indices, data, n_features, exc=RuntimeError)
     out = np.empty(csr.n_rows, dtype=np.float64)
     ex = L.exec_options()
     rc = L.lib().mfm_fm_predict_csr(csr, float(w0), L.ptr(w), L.ptr(v), v.shape[1], L.ptr(out),
@@ -91,10 +104,8 @@ def ffm_predict_cuda_csr(indptr, indices, data, n_features, field_ids, w0, w, v)
     if v.ndim != 3:
         raise ValueError(f"V must be 3-D (n_features, n_fields, k), got shape {v.shape}")
     _check_w_v(n_features, w, v.shape[0])
-    if field_ids.size != n_features:
-        raise ValueError(
-            f"field_ids length {field_ids.size} does not match n_features {n_features}")
-    csr, keep = L.make_csr(indptr, indices, data, n_features)
+    _check_field_ids(field_ids, n_features, v.shape[1])
+    csr, keep = L.make_csr(indptr, indices, data, n_features, exc=RuntimeError)
     out = np.empty(csr.n_rows, dtype=np.float64)
     rc = L.lib().mfm_ffm_predict_csr(csr, L.ptr(field_ids, L.i64p), v.shape[1], float(w0),
                                      L.ptr(w), L.ptr(v), v.shape[2], L.ptr(out),
@@ -112,10 +123,8 @@ def fwfm_predict_cuda_csr(indptr, indices, data, n_features, field_ids, w0, w, v
     if v.ndim != 2:
         raise ValueError(f"V must be 2-D (n_features, k), got shape {v.shape}")
     _check_w_v(n_features, w, v.shape[0])
-    if field_ids.size != n_features:
-        raise ValueError(
-            f"field_ids length {field_ids.size} does not match n_features {n_features}")
-    csr, keep = L.make_csr(indptr, indices, data, n_features)
+    _check_field_ids(field_ids, n_features, r.shape[0])
+    csr, keep = L.make_csr(indptr, indices, data, n_features, exc=RuntimeError)
     out = np.empty(csr.n_rows, dtype=np.float64)
     rc = L.lib().mfm_fwfm_predict_csr(csr, L.ptr(field_ids, L.i64p), r.shape[0], float(w0),
                                       L.ptr(w), L.ptr(v), L.ptr(r), v.shape[1], L.ptr(out),

@@ -140,10 +140,13 @@ def test_ffm_large_row():
 
 
 def test_predict_validation_on_device():
+    # the reference raises RuntimeError for everything inside the CUDA predict
+    # call, CSR checks included (rust/src/lib.rs:1506-1512), and ValueError for
+    # the field-id check that precedes it (lib.rs:1536-1537)
     ip, ix, dv = np.array([0, 1, 2]), np.array([0, 5]), np.ones(2)
-    with pytest.raises(ValueError, match=r"column index out of range \[0, 3\)"):
+    with pytest.raises(RuntimeError, match=r"column index out of range \[0, 3\)"):
         _rust.fm_predict_cuda_csr(ip, ix, dv, 3, 0.0, np.zeros(3), np.zeros((3, 2)))
-    with pytest.raises(ValueError, match="indptr must be non-decreasing"):
+    with pytest.raises(RuntimeError, match="indptr must be non-decreasing"):
         _rust.fm_predict_cuda_csr(np.array([0, 2, 1, 2]), np.array([0, 1]), np.ones(2), 3, 0.0,
                                   np.zeros(3), np.zeros((3, 2)))
     with pytest.raises(ValueError, match=r"field id out of range \[0, 2\)"):
