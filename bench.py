@@ -84,7 +84,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.idx), "-lms", "100"], stdout=subprocess.PIPE,
+                 "-i", str(self.idx), "-lms", "50"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -202,6 +202,8 @@ def run_ours(args):
     from modern_fm_b200 import _lib
     from modern_fm_b200 import workloads as WL
 
+    global N_ROWS
+    N_ROWS = args.rows
     rank, world, local = dist_setup(args.gpus)
     dev_t = torch.device("cuda", local)
     torch.cuda.set_device(dev_t)
@@ -228,6 +230,7 @@ def run_ours(args):
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -242,6 +245,11 @@ def run_ours(args):
     launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
     launch_ms = max_over_ranks(launch_ms, world)
     clocks = clk.summary()
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"kernel_only": True, "rows": N_ROWS, "launch_ms": launch_ms,
+                              "ms_per_step": total_ms / args.steps}), flush=True)
+        return
 
     # e2e through the C ABI with pinned host buffers in the boundary format
     Xh, keep = host_inputs(X)
@@ -364,8 +372,12 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--rows", type=int, default=N_ROWS,
+                    help="rows per GPU (smaller cases for profiling runs)")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="time only the device-resident kernel (profiling runs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     args = ap.parse_args()
     if args.impl == "reference":
