@@ -188,6 +188,28 @@ int mfm_fwfm_predict_device(int dtype, int device, const int64_t* indptr,
                             const void* w, const void* v, const void* r, int64_t k, void* out,
                             void* stream);
 
+/* ---- allocation-free FM scoring --------------------------------------------
+ * No counterpart in the reference: an addition for callers that cannot let
+ * the library allocate GPU memory, such as a host that owns the whole device
+ * budget through its own pool, or a latency-bound serving loop that cannot
+ * afford cudaMalloc / cudaFree (they may synchronise the device and stall
+ * every stream). Same arguments, results and errors as mfm_fm_predict_csr on
+ * ex->device (n_devices is ignored), but the CSR, parameters, validation flags
+ * and scores are staged in one static device array of
+ * mfm_noalloc_scratch_bytes() bytes (64 MiB) that every GPU loading this
+ * library holds until the process exits; no cudaMalloc, cudaFree or other
+ * allocating routine is called. Inputs whose staging does not fit return
+ * MFM_ERR_UNSUPPORTED before any device work. The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that first
+ * call before any stream capture. Calls share the array: each call clears the
+ * flags it needs, and calls that overlap on the GPU race on the array (the
+ * engine serialises calls on one device within a process). */
+int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const double* w, const double* v,
+                               int64_t k, double* out, const mfm_exec* ex);
+
+/* Size in bytes of the static array behind mfm_fm_predict_csr_noalloc. */
+int64_t mfm_noalloc_scratch_bytes(void);
+
 /* Release the engine's cached device memory on every device. */
 void mfm_release_cached_memory(void);
 

@@ -549,3 +549,23 @@ extern "C" int mfm_fwfm_predict_device(int dtype, int device, const int64_t* ind
             fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
     });
 }
+
+// ------------------------------------------- launchers for staged inputs --
+// FM scoring over device copies in the boundary layout (int64 indices,
+// float64 values), parameters in float64 or float32. Used by the
+// allocation-free entry point (predict_noalloc.cu), which stages its inputs in
+// its own static device buffer.
+namespace mfm {
+void fm_launch_staged_f64(int device, cudaStream_t s, const int64_t* indptr,
+                          const int64_t* indices, const double* data, int64_t n_rows,
+                          double w0, const double* w, const double* v, int k, double* out) {
+    fm_launch<double, int64_t, double, double>(device, s, indptr, indices, data, n_rows, 0, w0,
+                                               w, v, k, out);
+}
+void fm_launch_staged_f32(int device, cudaStream_t s, const int64_t* indptr,
+                          const int64_t* indices, const double* data, int64_t n_rows,
+                          double w0, const float* w, const float* v, int k, double* out) {
+    fm_launch<float, int64_t, double, double>(device, s, indptr, indices, data, n_rows, 0, w0,
+                                              w, v, k, out);
+}
+}  // namespace mfm
