@@ -99,6 +99,96 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Row-group FM kernel for latent rows of up to 16 vectors: LR lanes score one
+// row (32/LR rows per warp); a nonzero's latent row is spread over L lanes
+// (VEC elements each, 16-byte loads), G = LR/L nonzeros per step. One
+// iteration covers CAP nonzeros: their indices and values are loaded by the
+// row's lanes at once, w is gathered lane-parallel, and all CAP/G latent-row
+// gathers are issued before any of them is consumed, so a 39-nonzero row makes
+// three dependent memory round trips (indptr, index slice, gathers).
+template <class T, class IdxT, class ValT, class OutT, int VEC, int L, int LR, int CAP, int MINB>
+__global__ void __launch_bounds__(256, MINB)
+    fm_rows_kernel(const int64_t* __restrict__ indptr, const IdxT* __restrict__ indices,
+                   const ValT* __restrict__ data, int64_t n_rows, int64_t nnz_base, T w0,
+                   const T* __restrict__ w, const T* __restrict__ v, int k,
+                   OutT* __restrict__ out) {
+    constexpr int G = LR / L;     // nonzeros per step
+    constexpr int NC = CAP / LR;  // index chunks per iteration
+    constexpr int S = CAP / G;    // hoisted gather steps per iteration
+    static_assert(LR % L == 0 && CAP % LR == 0 && 32 % LR == 0, "row-group shape");
+    const int lane = threadIdx.x & 31, rl = lane & (LR - 1), grp = rl / L, l = rl % L;
+    const bool act = l < k / VEC;
+    const int64_t nslots = ((int64_t)gridDim.x * blockDim.x) / LR;
+    for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR;; row += nslots) {
+        const bool live = row < n_rows;
+        if (!__any_sync(kFull, live)) break;
+        const int64_t b = live ? indptr[row] - nnz_base : 0;
+        const int64_t e = live ? indptr[row + 1] - nnz_base : 0;
+        T acc[VEC];
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) acc[c] = T(0);
+        T sq = T(0), lin = T(0);
+        for (int64_t base = b;; base += CAP) {
+            const bool more = base < e;
+            if (!__any_sync(kFull, more)) break;
+            int nh[NC];
+            IdxT ii[NC];
+            T xx[NC];
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int64_t rem = e - base - LR * c;
+                nh[c] = !more || rem <= 0 ? 0 : (rem >= LR ? LR : (int)rem);
+                ii[c] = 0;
+                xx[c] = T(0);
+                if (rl < nh[c]) {
+                    ii[c] = indices[base + LR * c + rl];
+                    xx[c] = (T)data[base + LR * c + rl];
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                if (rl < nh[c]) lin += w[ii[c]] * xx[c];
+            Vec<T, VEC> q[S];
+            T xs[S];
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                const int c = s / L, src = (s % L) * G + grp;
+                const IdxT i = __shfl_sync(kFull, ii[c], src, LR);
+                const T x = __shfl_sync(kFull, xx[c], src, LR);
+                const bool ok = src < nh[c];
+                xs[s] = ok ? x : T(0);
+                if (ok && act) {
+                    q[s] = ldg_vec<T, VEC>(v + (int64_t)i * k + l * VEC);
+                } else {
+#pragma unroll
+                    for (int cc = 0; cc < VEC; ++cc) q[s].v[cc] = T(0);
+                }
+            }
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+#pragma unroll
+                for (int cc = 0; cc < VEC; ++cc) {
+                    const T vx = q[s].v[cc] * xs[s];
+                    acc[cc] += vx;
+                    sq += vx * vx;
+                }
+        }
+#pragma unroll
+        for (int o = L; o < LR; o <<= 1)
+#pragma unroll
+            for (int cc = 0; cc < VEC; ++cc) acc[cc] += __shfl_xor_sync(kFull, acc[cc], o);
+        T pair = T(0);
+        if (grp == 0 && act) {
+#pragma unroll
+            for (int cc = 0; cc < VEC; ++cc) pair += acc[cc] * acc[cc];
+        }
+        T t = lin + T(0.5) * (pair - sq);
+#pragma unroll
+        for (int o = LR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
+        if (rl == 0 && live) out[row] = (OutT)(w0 + t);
+    }
+}
+
 // The row's upper-triangle pair list (a < b, a ascending then b ascending, the
 // reference's order, rust/src/ffm.rs:32-43) is walked 32 entries at a time:
 // each lane advances its (a, b) cursor by 32 positions.
@@ -231,11 +321,42 @@ void fm_launch_vec(unsigned grid, cudaStream_t s, const int64_t* indptr, const I
     fail(MFM_ERR_UNSUPPORTED, fmt("k=%d exceeds the FM kernel's register tiling", k));
 }
 
+// Row-group shapes (see fm_rows_kernel): returns false when k needs the
+// generic kernel. Gathers hoisted per iteration stay at <= 48 registers.
+template <class T, class IdxT, class ValT, class OutT>
+bool fm_rows_launch(int device, cudaStream_t s, const int64_t* indptr, const IdxT* indices,
+                    const ValT* data, int64_t n_rows, int64_t nnz_base, T w0, const T* w,
+                    const T* v, int k, OutT* out) {
+    constexpr int V = 16 / (int)sizeof(T);  // 4 floats or 2 doubles per 16-byte load
+    if (k % V != 0) return false;
+    const int nvec = k / V;
+    const unsigned grid = (unsigned)sm_count(device) * 8;
+#define MFM_ROWS(L_, LR_, CAP_, MB_)                                                       \
+    {                                                                                      \
+        const int64_t slots = (int64_t)grid * 256 / LR_;                                   \
+        const unsigned g = (unsigned)std::max<int64_t>(                                    \
+            1, std::min<int64_t>(grid, ceil_div(std::min(n_rows, slots) * LR_, 256)));     \
+        fm_rows_kernel<T, IdxT, ValT, OutT, V, L_, LR_, CAP_, MB_><<<g, 256, 0, s>>>(       \
+            indptr, indices, data, n_rows, nnz_base, w0, w, v, k, out);                    \
+        return true;                                                                       \
+    }
+    if (nvec <= 2) MFM_ROWS(2, 16, 48, 4)
+    if (nvec <= 4) MFM_ROWS(4, 16, 48, 4)
+    if (nvec <= 8) MFM_ROWS(8, 32, 32, 4)
+#undef MFM_ROWS
+    return false;
+}
+
 template <class T, class IdxT, class ValT, class OutT>
 void fm_launch(int device, cudaStream_t s, const int64_t* indptr, const IdxT* indices,
                const ValT* data, int64_t n_rows, int64_t nnz_base, double w0, const T* w,
                const T* v, int k, OutT* out) {
     if (n_rows <= 0) return;
+    if (fm_rows_launch<T, IdxT, ValT, OutT>(device, s, indptr, indices, data, n_rows, nnz_base,
+                                            (T)w0, w, v, k, out)) {
+        MFM_CHECK_LAUNCH("FM predict launch");
+        return;
+    }
     const unsigned grid = warp_grid(device, n_rows, kWarpsPerBlock, kBlocksPerSm);
     switch (vec_width<T>(k)) {
     case 4:

@@ -62,14 +62,25 @@ def test_predict_golden_f32(case, f32):
     assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-5 * scale)
 
 
-@pytest.mark.parametrize("k", [1, 3, 4, 16, 17, 64, 130, 1024])
-def test_fm_predict_k_range(k):
+@pytest.mark.parametrize("k", [1, 2, 3, 4, 8, 12, 16, 17, 24, 32, 64, 130, 1024])
+@pytest.mark.parametrize("dtype", ["float64", "float32"])
+def test_fm_predict_k_range(k, dtype, monkeypatch):
+    """Every latent width reaches a kernel shape (row-group or generic); rows
+    of 0 to 150 nonzeros cover one and several gather iterations."""
+    monkeypatch.setenv("MFM_B200_DTYPE", dtype)
     rng = np.random.default_rng(k)
-    ip, ix, dv = _random_csr(rng, 300, 60, 0.2)
-    w0, w, V = rng.normal(), rng.normal(size=60), rng.normal(size=(60, k))
-    want = O.fm_predict_fast_csr(ip, ix, dv, 60, w0, w, V)
-    got = _rust.fm_predict_cuda_csr(ip, ix, dv, 60, w0, w, V)
-    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=1e-9 * max(1.0, k / 16))
+    ip, ix, dv = _random_csr(rng, 300, 200, 0.2)
+    ip2, ix2, dv2 = _random_csr(rng, 20, 200, 0.75)  # ~150 nonzeros per row
+    ip = np.concatenate([ip, ip2[1:] + ip[-1]])
+    ix, dv = np.concatenate([ix, ix2]), np.concatenate([dv, dv2])
+    w0, w, V = rng.normal(), rng.normal(size=200), rng.normal(size=(200, k)) * 0.3
+    want = O.fm_predict_fast_csr(ip, ix, dv, 200, w0, w, V)
+    got = _rust.fm_predict_cuda_csr(ip, ix, dv, 200, w0, w, V)
+    if dtype == "float64":
+        np.testing.assert_allclose(got, want, rtol=RTOL64, atol=1e-9 * max(1.0, k / 16))
+    else:
+        scale = _scale_fm(ip, ix, dv, w0, w, V)
+        assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-5 * scale)
 
 
 def test_empty_rows_and_single_nonzero():
