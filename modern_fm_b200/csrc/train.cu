@@ -18,13 +18,18 @@
 //     count -> scan -> expand (key, batch-local entry id) -> segmented stable
 //     radix sort by key within each batch -> run detection -> work items of
 //     <= kItem entries per run;
+//     plus one 16-byte descriptor per work item and the inverse permutation
+//     (entry -> sorted position);
 //   per batch:
-//     forward kernel (warp per row): scores, loss gradient, per-entry gradient
-//       payloads (all classes);
-//     stage 1 (warp per work item): sums payload rows of its entries in sorted
-//       order; single-item runs apply the optimizer at once;
-//     stage 2 (warp per multi-item run): combines item partials in order and
-//       applies; one extra block steps w0 from the per-row gradients.
+//     forward kernel (rows): scores, loss gradient, and each entry's gradient
+//       payload (all classes) written straight to its sorted position, rows
+//       padded to 16 bytes;
+//     stage 1 (several work items per warp, 16-byte column vectors): sums the
+//       contiguous payload rows of each item; single-item runs apply the
+//       optimizer at once;
+//     stage 2 (warp per multi-item run): combines the item partials in a
+//       fixed order and applies; its last block steps w0 from the per-row
+//       gradients.
 #include <algorithm>
 #include <cmath>
 
@@ -100,6 +105,88 @@ __device__ __forceinline__ void opt_step(const GroupDev<T>& g, int64_t idx, T dg
     }
     g.p[idx] = th;
 }
+
+// opt_step on VEC consecutive coordinates [idx0, idx0 + VEC) of one group,
+// with 16-byte loads and stores of the parameter and its state. The state is
+// loaded before the gradients are known (`prefetch`) so the loads overlap the
+// payload reduction; `commit` applies the step.
+template <class T, int VEC>
+struct VecStep {
+    Vec<T, VEC> p, a, b, c;  // param and up to three state vectors
+    __device__ __forceinline__ void prefetch(const GroupDev<T>& g, int64_t idx0, int kind) {
+        p = ldg_vec<T, VEC>(g.p + idx0);
+        if (kind == MFM_OPT_ADAGRAD) {
+            a = ldg_vec<T, VEC>(g.acc + idx0);
+        } else if (kind == MFM_OPT_ADAM) {
+            a = ldg_vec<T, VEC>(g.m + idx0);
+            b = ldg_vec<T, VEC>(g.s + idx0);
+            c = ldg_vec<T, VEC>(g.t + idx0);
+        } else if (kind == MFM_OPT_FTRL) {
+            a = ldg_vec<T, VEC>(g.z + idx0);
+            b = ldg_vec<T, VEC>(g.n + idx0);
+        }
+    }
+    __device__ __forceinline__ void commit(const GroupDev<T>& g, int64_t idx0, const T* dg,
+                                           const OptDev& o) {
+        const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) {
+            T th = p.v[u];
+            switch (o.kind) {
+            case MFM_OPT_SGD:
+                th -= lr * (dg[u] + l2 * th);
+                break;
+            case MFM_OPT_ADAGRAD: {
+                const T gr = dg[u] + l2 * th;
+                const T ac = a.v[u] + gr * gr;
+                a.v[u] = ac;
+                th -= lr * gr / sqrt(ac + (T)1e-10);
+                break;
+            }
+            case MFM_OPT_ADAM: {
+                const T gr = dg[u] + l2 * th;
+                const T b1 = (T)o.b1, b2 = (T)o.b2;
+                const T t = c.v[u] + T(1);
+                const T m = b1 * a.v[u] + (T(1) - b1) * gr;
+                const T v = b2 * b.v[u] + (T(1) - b2) * gr * gr;
+                c.v[u] = t;
+                a.v[u] = m;
+                b.v[u] = v;
+                const T mh = m / (T(1) - pow(b1, t));
+                const T vh = v / (T(1) - pow(b2, t));
+                th -= lr * mh / (sqrt(vh) + (T)o.eps);
+                break;
+            }
+            default: {
+                const T d = dg[u];
+                const T n = b.v[u], nn = n + d * d;
+                const T sigma = (sqrt(nn) - sqrt(n)) / lr;
+                const T z = a.v[u] + d - sigma * th;
+                a.v[u] = z;
+                b.v[u] = nn;
+                if (fabs(z) <= l1)
+                    th = T(0);
+                else {
+                    const T sign = z < T(0) ? T(-1) : T(1);
+                    th = -(z - sign * l1) / (((T)o.fbeta + sqrt(nn)) / lr + l2);
+                }
+            }
+            }
+            p.v[u] = th;
+        }
+        *reinterpret_cast<Vec<T, VEC>*>(g.p + idx0) = p;
+        if (o.kind == MFM_OPT_ADAGRAD) {
+            *reinterpret_cast<Vec<T, VEC>*>(g.acc + idx0) = a;
+        } else if (o.kind == MFM_OPT_ADAM) {
+            *reinterpret_cast<Vec<T, VEC>*>(g.m + idx0) = a;
+            *reinterpret_cast<Vec<T, VEC>*>(g.s + idx0) = b;
+            *reinterpret_cast<Vec<T, VEC>*>(g.t + idx0) = c;
+        } else if (o.kind == MFM_OPT_FTRL) {
+            *reinterpret_cast<Vec<T, VEC>*>(g.z + idx0) = a;
+            *reinterpret_cast<Vec<T, VEC>*>(g.n + idx0) = b;
+        }
+    }
+};
 
 // --------------------------------------------------------- layout moves --
 
@@ -238,6 +325,41 @@ __global__ void items_kernel(const int64_t* __restrict__ item_start,
     for (int64_t i = i0; i < i1; ++i) item_run[i] = r;
     if (i1 - i0 > 1) long_list[long_scan[r]] = r;
 }
+// One 16-byte descriptor per work item: first sorted entry (epoch index),
+// entry count (bit 31 set when the run has several items) and key.
+struct ItemDesc {
+    int64_t p0;
+    uint32_t cnt;
+    uint32_t key;
+};
+constexpr uint32_t kMultiItem = 0x80000000u;
+
+__global__ void desc_kernel(const int64_t* __restrict__ item_run,
+                            const int64_t* __restrict__ item_start,
+                            const int64_t* __restrict__ run_start,
+                            const uint32_t* __restrict__ keys, int64_t I,
+                            ItemDesc* __restrict__ desc) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= I) return;
+    const int64_t r = item_run[i], i0 = item_start[r], i1 = item_start[r + 1];
+    const int64_t rs = run_start[r], re = run_start[r + 1];
+    const int64_t p0 = rs + (i - i0) * kItem;
+    const int64_t cnt = re - p0 < kItem ? re - p0 : kItem;
+    ItemDesc d;
+    d.p0 = p0;
+    d.cnt = (uint32_t)cnt | (i1 - i0 > 1 ? kMultiItem : 0u);
+    d.key = keys[rs];
+    desc[i] = d;
+}
+
+// inv[seg_lo[b] + e] = sorted position (batch-local) of batch b's entry e.
+__global__ void inverse_kernel(const int64_t* __restrict__ seg_lo,
+                               const uint32_t* __restrict__ vals, uint32_t* __restrict__ inv) {
+    const int64_t b = blockIdx.x, s0 = seg_lo[b], s1 = seg_lo[b + 1];
+    for (int64_t p = s0 + threadIdx.x; p < s1; p += blockDim.x)
+        inv[s0 + vals[p]] = (uint32_t)(p - s0);
+}
+
 __global__ void batch_tables_kernel(const int64_t* __restrict__ seg_lo, int64_t nb,
                                     const int64_t* __restrict__ run_id,
                                     const int64_t* __restrict__ item_start,
@@ -270,8 +392,10 @@ struct FwdArgs {
     T ls_on, ls_off;  // softmax targets: 1 - eps for the true class, eps / (C - 1) otherwise
     const T *w0, *w, *v, *r;
     const int32_t* fid;
+    const uint32_t* inv1;  // entry -> batch-local sorted position, stream 1
+    const uint32_t* inv2;  // stream 2
     T* pay1;
-    int W1;
+    int W1;  // padded payload row stride (multiple of 16 bytes), stream 1
     T* pay2;
     int W2;
     T* grow;  // (nrows, C) per-row loss gradients, summed into the w0 gradient
@@ -309,9 +433,9 @@ __device__ __forceinline__ void row_gradients(const FwdArgs<T>& A, int64_t row, 
     }
 }
 
-// FM (binary and multiclass): D = C*k latent columns per feature, split over
-// Lc lanes (G = 32/Lc nonzeros per warp step), MCOL columns per lane.
-// Payload per nonzero: [g_c x (C) | g_c (x cache_cf - v_cf x^2) (C*k)]
+// FM (binary and multiclass), any width: D = C*k latent columns per feature,
+// split over Lc lanes (G = 32/Lc nonzeros per warp step), MCOL columns per
+// lane. Payload per nonzero: [g_c (x cache_cf - v_cf x^2) (C*k) | g_c x (C)]
 // (FmGradAccum::add_row, rust/src/fm.rs:133-146).
 template <class T, int MCOL>
 __global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) {
@@ -399,17 +523,157 @@ __global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) 
                 const T x = __shfl_sync(0xffffffffu, my_x, src);
                 if (src < nh) {
                     const T* vi = A.v + (int64_t)i * D;
-                    T* P = A.pay1 + (e0 + base + src) * A.W1;
-                    if (l < C) P[l] = gs[l] * x;
+                    T* P = A.pay1 + (int64_t)A.inv1[A.seg1 + e0 + base + src] * A.W1;
+                    if (l < C) P[D + l] = gs[l] * x;
 #pragma unroll
                     for (int m = 0; m < MCOL; ++m) {
                         const int jj = l + m * Lc;
-                        if (jj < D) P[C + jj] = gs[jj / k] * (x * cache[m] - vi[jj] * x * x);
+                        if (jj < D) P[jj] = gs[jj / k] * (x * cache[m] - vi[jj] * x * x);
                     }
                 }
             }
         }
         __syncwarp();
+    }
+}
+
+// Binary FM, latent rows of up to 8 vectors (k <= 32 float32, k <= 16
+// float64): LR lanes per row, L lanes per nonzero (VEC-wide loads), CAP
+// nonzeros per iteration with every gather issued before use (as in the
+// scoring kernel). Rows that fit one iteration keep their gathered latent rows
+// in registers for the payload pass; longer rows gather again.
+template <class T, int VEC, int L, int LR, int CAP>
+struct RowsShape {
+    static constexpr int G = LR / L, NC = CAP / LR, S = CAP / G;
+};
+
+template <class T, int VEC, int L, int LR, int CAP>
+__device__ __forceinline__ void rows_gather(const FwdArgs<T>& A, int64_t rb, int64_t z,
+                                            int64_t base, int rl, int grp, int l, bool act,
+                                            int (&nh)[RowsShape<T, VEC, L, LR, CAP>::NC],
+                                            Vec<T, VEC> (&q)[RowsShape<T, VEC, L, LR, CAP>::S],
+                                            T (&xs)[RowsShape<T, VEC, L, LR, CAP>::S], T& lin) {
+    using Sh = RowsShape<T, VEC, L, LR, CAP>;
+    int32_t ii[Sh::NC];
+    T xx[Sh::NC];
+#pragma unroll
+    for (int c = 0; c < Sh::NC; ++c) {
+        const int64_t rem = z - base - LR * c;
+        nh[c] = rem <= 0 ? 0 : (rem >= LR ? LR : (int)rem);
+        ii[c] = 0;
+        xx[c] = T(0);
+        if (rl < nh[c]) {
+            ii[c] = A.indices[rb + base + LR * c + rl];
+            xx[c] = A.data[rb + base + LR * c + rl];
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < Sh::NC; ++c)
+        if (rl < nh[c]) lin += A.w[ii[c]] * xx[c];
+#pragma unroll
+    for (int st = 0; st < Sh::S; ++st) {
+        const int c = st / L, src = (st % L) * Sh::G + grp;
+        const int32_t i = __shfl_sync(0xffffffffu, ii[c], src, LR);
+        const T x = __shfl_sync(0xffffffffu, xx[c], src, LR);
+        const bool ok = src < nh[c];
+        xs[st] = ok ? x : T(0);
+        if (ok && act) {
+            q[st] = ldg_vec<T, VEC>(A.v + (int64_t)i * A.k + l * VEC);
+        } else {
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) q[st].v[u] = T(0);
+        }
+    }
+}
+
+template <class T, int VEC, int L, int LR, int CAP>
+__device__ __forceinline__ void rows_payload(const FwdArgs<T>& A, int64_t e0, int64_t base,
+                                             int grp, int l, bool act, T g, const T* cache,
+                                             const int (&nh)[RowsShape<T, VEC, L, LR, CAP>::NC],
+                                             const Vec<T, VEC> (&q)[RowsShape<T, VEC, L, LR, CAP>::S],
+                                             const T (&xs)[RowsShape<T, VEC, L, LR, CAP>::S]) {
+    using Sh = RowsShape<T, VEC, L, LR, CAP>;
+#pragma unroll
+    for (int st = 0; st < Sh::S; ++st) {
+        const int c = st / L, src = (st % L) * Sh::G + grp;
+        if (src >= nh[c]) continue;
+        const int64_t a = base + LR * c + src;
+        T* P = A.pay1 + (int64_t)A.inv1[A.seg1 + e0 + a] * A.W1;
+        const T x = xs[st];
+        if (act) {
+            Vec<T, VEC> o;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) o.v[u] = g * (x * cache[u] - q[st].v[u] * x * x);
+            *reinterpret_cast<Vec<T, VEC>*>(P + l * VEC) = o;
+        }
+        if (l == 0) P[A.k] = g * x;  // w column after the k latent columns
+    }
+}
+
+template <class T, int VEC, int L, int LR, int CAP>
+__global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
+    using Sh = RowsShape<T, VEC, L, LR, CAP>;
+    const int lane = threadIdx.x & 31, rl = lane & (LR - 1), grp = rl / L, l = rl % L;
+    const bool act = l < A.k / VEC;
+    const int64_t nslots = ((int64_t)gridDim.x * blockDim.x) / LR;
+    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR;; j += nslots) {
+        const bool live = j < A.nrows;
+        if (!__any_sync(0xffffffffu, live)) break;
+        const int64_t pos = A.pos0 + j;
+        const int64_t row = live ? A.order[pos] : 0;
+        const int64_t rb = live ? A.indptr[row] : 0;
+        const int64_t z = live ? A.indptr[row + 1] - rb : 0;
+        // pass 1: score from the frozen parameters (train_score_row, fm.rs:77-101)
+        T cache[VEC];
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) cache[u] = T(0);
+        T sq = T(0), lin = T(0);
+        int nh[Sh::NC];
+        Vec<T, VEC> q[Sh::S];
+        T xs[Sh::S];
+        int iters = 0;
+        for (int64_t base = 0;; base += CAP, ++iters) {
+            if (!__any_sync(0xffffffffu, base < z)) break;
+            rows_gather<T, VEC, L, LR, CAP>(A, rb, z, base, rl, grp, l, act, nh, q, xs, lin);
+#pragma unroll
+            for (int st = 0; st < Sh::S; ++st)
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) {
+                    const T vx = q[st].v[u] * xs[st];
+                    cache[u] += vx;
+                    sq += vx * vx;
+                }
+        }
+#pragma unroll
+        for (int o = L; o < LR; o <<= 1)
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) cache[u] += __shfl_xor_sync(0xffffffffu, cache[u], o);
+        T pair = T(0);
+        if (grp == 0 && act) {
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) pair += cache[u] * cache[u];
+        }
+        T t = lin + T(0.5) * (pair - sq);
+#pragma unroll
+        for (int o = LR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+        T g = T(0);
+        if (live) {  // loss_grad x sample_weight, optimizer.rs:38-43
+            const T s = A.w0[0] + t, y = A.y[row];
+            g = A.sw[row] * (A.loss == MFM_LOSS_LOGISTIC ? sigmoid_t(s) - y : s - y);
+            if (rl == 0) A.grow[j] = g;
+        }
+        // pass 2: payload rows at their sorted positions
+        const int64_t e0 = live ? A.estart1[pos] - A.seg1 : 0;
+        if (iters == 1) {
+            rows_payload<T, VEC, L, LR, CAP>(A, e0, 0, grp, l, act, g, cache, nh, q, xs);
+        } else {
+            for (int64_t base = 0;; base += CAP) {
+                if (!__any_sync(0xffffffffu, base < z)) break;
+                T dummy = T(0);
+                rows_gather<T, VEC, L, LR, CAP>(A, rb, z, base, rl, grp, l, act, nh, q, xs, dummy);
+                rows_payload<T, VEC, L, LR, CAP>(A, e0, base, grp, l, act, g, cache, nh, q, xs);
+            }
+        }
     }
 }
 
@@ -462,7 +726,7 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
         for (int64_t q = lane; q < z * C; q += 32) {
             const int64_t a = q / C;
             const int c = (int)(q - a * C);
-            A.pay1[(e1 + a) * C + c] = gs[c] * dv[a];
+            A.pay1[(int64_t)A.inv1[A.seg1 + e1 + a] * A.W1 + c] = gs[c] * dv[a];
         }
         const int64_t e2 = A.estart2[pos] - A.seg2;
         const int64_t tot = z * (z - 1) * CK;
@@ -473,7 +737,7 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
             const int c = col / k, t = col - c * k;
             const int32_t ib = ix[b];
             const int fa = A.fid[ix[a]];
-            A.pay2[(e2 + pe) * CK + col] =
+            A.pay2[(int64_t)A.inv2[A.seg2 + e2 + pe] * A.W2 + col] =
                 gs[c] * dv[a] * dv[b] * A.v[(((int64_t)ib * F + fa) * C + c) * k + t];
         }
         __syncwarp();
@@ -487,7 +751,7 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
 template <class T, int VEC>
 __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
     extern __shared__ unsigned char smraw[];
-    const int C = A.C, k = A.k, F = A.F, W1 = A.W1;
+    const int C = A.C, k = A.k, F = A.F, W1 = A.W1, CK = C * k;
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     T* logit = reinterpret_cast<T*>(smraw) + (size_t)wib * 2 * C;
     T* gs = logit + C;
@@ -527,14 +791,15 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
         __syncwarp();
         for (int c = lane; c < C; c += 32) A.grow[j * C + c] = gs[c];
         const int64_t e1 = A.estart1[pos] - A.seg1;
-        for (int64_t q = lane; q < z * W1; q += 32) {
-            const int64_t a = q / W1;
-            const int col = (int)(q - a * W1);
+        const int W1u = CK + C;  // used columns: [v (C*k) | w (C)]
+        for (int64_t q = lane; q < z * W1u; q += 32) {
+            const int64_t a = q / W1u;
+            const int col = (int)(q - a * W1u);
             T val;
-            if (col < C) {
-                val = gs[col] * dv[a];
+            if (col >= CK) {
+                val = gs[col - CK] * dv[a];
             } else {
-                const int jj = col - C, c = jj / k, t = jj - c * k;
+                const int c = col / k, t = col - c * k;
                 const int fa = A.fid[ix[a]];
                 T s = T(0);
                 for (int64_t b = 0; b < z; ++b) {
@@ -546,7 +811,7 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
                 }
                 val = gs[c] * dv[a] * s;
             }
-            A.pay1[(e1 + a) * W1 + col] = val;
+            A.pay1[(int64_t)A.inv1[A.seg1 + e1 + a] * W1 + col] = val;
         }
         const int64_t e2 = A.estart2[pos] - A.seg2;
         int64_t a = 0, b = 1 + lane, pi = lane;
@@ -559,7 +824,7 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
                 const T* pb = A.v + ((int64_t)ib * C + c) * k;
                 T dot = T(0);
                 for (int t = 0; t < k; ++t) dot += pa[t] * pb[t];
-                A.pay2[(e2 + pi) * C + c] = gs[c] * xab * dot;
+                A.pay2[(int64_t)A.inv2[A.seg2 + e2 + pi] * A.W2 + c] = gs[c] * xab * dot;
             }
             b += 32;
             pi += 32;
@@ -573,19 +838,23 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
 
 template <class T>
 struct RedArgs {
-    const uint32_t* keys;  // sorted keys of the epoch
-    const uint32_t* vals;  // batch-local entry ids, in sorted order
-    const int64_t* run_start;
-    const int64_t* item_start;
-    const int64_t* item_run;
-    const int64_t* long_list;
-    const T* pay;
-    T* part;
-    int W;
-    int cb1;  // first column of group 1 (== W when there is one group)
+    const ItemDesc* desc;       // this batch's items start at desc[item0]
+    const int64_t* item_start;  // per run
+    const int64_t* long_list;   // runs with several items
+    const T* pay;               // batch payload rows in sorted order, stride Wp
+    T* part;                    // item partials (batch-local item index), stride Wp
+    int W, Wp, cb1;             // used columns, row stride, first column of group 1
+    int nv, nvs, gpw;           // vectors per row, vectors per lane group, groups per warp
+    int vec0;                   // 1: vectors lying inside group 0 step with 16-byte accesses
+    int64_t seg, item0;
     GroupDev<T> g0, g1;
     OptDev opt;
     T inv_bsz;
+    // w0 step (last block of stage 2)
+    const T* grow;
+    int64_t nrows;
+    int C, do_w0;
+    GroupDev<T> gw0;
 };
 
 template <class T>
@@ -596,83 +865,176 @@ __device__ __forceinline__ void apply_col(const RedArgs<T>& R, uint32_t key, int
         opt_step(R.g1, (int64_t)key * R.g1.width + (col - R.cb1), sum * R.inv_bsz, R.opt);
 }
 
-// Stage 1: one warp per work item (<= kItem sorted entries of one run).
-template <class T, int MW>
-__global__ void __launch_bounds__(256)
-    reduce_stage1_kernel(RedArgs<T> R, int64_t item0, int64_t item1) {
-    const int lane = threadIdx.x & 31;
-    const int64_t it = item0 + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (it >= item1) return;
-    const int64_t r = R.item_run[it];
-    const int64_t i0 = R.item_start[r], npieces = R.item_start[r + 1] - i0;
-    const int64_t rs = R.run_start[r], re = R.run_start[r + 1];
-    const int64_t p0 = rs + (it - i0) * kItem;
-    const int cnt = (int)min((int64_t)kItem, re - p0);
-    const uint32_t key = R.keys[rs];
-    const uint32_t my_e = lane < cnt ? R.vals[p0 + lane] : 0u;
-    for (int cb = 0; cb < R.W; cb += 32 * MW) {
-        T acc[MW];
+// Applies one VEC-wide column vector `vv` of key `key`: 16-byte accesses when
+// the vector lies inside group 0 (the latent columns), scalar steps otherwise.
+template <class T, int VEC>
+__device__ __forceinline__ bool vec_in_group0(const RedArgs<T>& R, int vv) {
+    return R.vec0 && (vv + 1) * VEC <= R.cb1;
+}
+
+// Stage 1: lane groups of nvs lanes, gpw groups per warp, one work item per
+// group; each lane sums VEC-wide column vectors over the item's contiguous
+// payload rows. Items of single-item runs apply the optimizer directly.
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t n_items) {
+    const int lane = threadIdx.x & 31, grp = lane / R.nvs, vl = lane % R.nvs;
+    if (grp >= R.gpw) return;
+    const int64_t it = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * R.gpw + grp;
+    if (it >= n_items) return;
+    const ItemDesc d = R.desc[R.item0 + it];
+    const int cnt = (int)(d.cnt & ~kMultiItem);
+    const bool multi = (d.cnt & kMultiItem) != 0;
+    const T* rows = R.pay + (d.p0 - R.seg) * R.Wp;
+    for (int vv = vl; vv < R.nv; vv += R.nvs) {
+        const bool vec = !multi && vec_in_group0<T, VEC>(R, vv);
+        const int64_t idx0 = (int64_t)d.key * R.g0.width + vv * VEC;
+        VecStep<T, VEC> st;
+        if (vec) st.prefetch(R.g0, idx0, R.opt.kind);  // overlaps the payload loads
+        T acc[VEC];
 #pragma unroll
-        for (int m = 0; m < MW; ++m) acc[m] = T(0);
+        for (int c = 0; c < VEC; ++c) acc[c] = T(0);
 #pragma unroll 4
         for (int q = 0; q < cnt; ++q) {
-            const T* row = R.pay + (int64_t)__shfl_sync(0xffffffffu, my_e, q) * R.W;
+            const Vec<T, VEC> x = ldg_vec<T, VEC>(rows + (int64_t)q * R.Wp + vv * VEC);
 #pragma unroll
-            for (int m = 0; m < MW; ++m) {
-                const int col = cb + lane + 32 * m;
-                if (col < R.W) acc[m] += row[col];
+            for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+        }
+        if (multi) {
+            Vec<T, VEC> o;
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) o.v[c] = acc[c];
+            *reinterpret_cast<Vec<T, VEC>*>(R.part + it * R.Wp + vv * VEC) = o;
+        } else if (vec) {
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) acc[c] *= R.inv_bsz;
+            st.commit(R.g0, idx0, acc, R.opt);
+        } else {
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) {
+                const int col = vv * VEC + c;
+                if (col < R.W) apply_col(R, d.key, col, acc[c]);
             }
         }
-#pragma unroll
-        for (int m = 0; m < MW; ++m) {
-            const int col = cb + lane + 32 * m;
-            if (col >= R.W) continue;
-            if (npieces == 1)
-                apply_col(R, key, col, acc[m]);
-            else
-                R.part[(it - item0) * R.W + col] = acc[m];
-        }
     }
 }
 
-// Stage 2: one warp per run longer than kItem: item partials in order.
-template <class T>
-__global__ void __launch_bounds__(256)
-    reduce_stage2_kernel(RedArgs<T> R, int64_t long0, int64_t long1, int64_t item0) {
-    const int lane = threadIdx.x & 31;
-    const int64_t li = long0 + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-    if (li >= long1) return;
-    const int64_t r = R.long_list[li];
-    const int64_t i0 = R.item_start[r], i1 = R.item_start[r + 1];
-    const uint32_t key = R.keys[R.run_start[r]];
-    for (int col = lane; col < R.W; col += 32) {
-        T s = T(0);
-        for (int64_t it = i0; it < i1; ++it) s += R.part[(it - item0) * R.W + col];
-        apply_col(R, key, col, s);
-    }
-}
-
-// w0: the batch's per-row gradients summed in a fixed tree, then one step.
-template <class T>
-__global__ void __launch_bounds__(256)
-    w0_kernel(const T* __restrict__ grow, int64_t nrows, int C, GroupDev<T> g, OptDev o,
-              T inv_bsz) {
+// Stage 2: one block per multi-item run. 8 warps x gp lane groups take the
+// run's item partials in a fixed stride, a shuffle tree folds the groups of a
+// warp and shared memory folds the warps in order, then the run is applied.
+// The last block steps w0 from the batch's per-row gradients (fixed tree).
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t l0, int64_t n_long) {
     __shared__ T sm[256];
-    for (int c = 0; c < C; ++c) {
-        T s = T(0);
-        for (int64_t j = threadIdx.x; j < nrows; j += 256) s += grow[j * C + c];
-        sm[threadIdx.x] = s;
-        __syncthreads();
-        for (int h = 128; h > 0; h >>= 1) {
-            if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
+    __shared__ __align__(16) T wsum[8][32 * VEC];
+    if (blockIdx.x == gridDim.x - 1) {
+        if (!R.do_w0) return;
+        for (int c = 0; c < R.C; ++c) {
+            T s = T(0);
+            for (int64_t j = threadIdx.x; j < R.nrows; j += 256) s += R.grow[j * R.C + c];
+            sm[threadIdx.x] = s;
+            __syncthreads();
+            for (int h = 128; h > 0; h >>= 1) {
+                if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
+                __syncthreads();
+            }
+            if (threadIdx.x == 0) opt_step(R.gw0, c, sm[0] * R.inv_bsz, R.opt);
             __syncthreads();
         }
-        if (threadIdx.x == 0) opt_step(g, c, sm[0] * inv_bsz, o);
+        return;
+    }
+    const int64_t li = blockIdx.x;
+    if (li >= n_long) return;  // uniform per block
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t r = R.long_list[l0 + li];
+    const int64_t i0 = R.item_start[r] - R.item0, i1 = R.item_start[r + 1] - R.item0;
+    const uint32_t key = R.desc[R.item0 + i0].key;
+    int gp = 1;  // power-of-two group count per warp for the shuffle fold
+    while (gp * 2 * R.nvs <= 32) gp *= 2;
+    const int grp = lane / R.nvs, vl = lane % R.nvs;
+    const bool in = grp < gp;
+    const int stride = gp * 8, slot = warp * gp + grp;
+    for (int vb = 0; vb < R.nv; vb += R.nvs) {
+        const int vv = vb + vl;
+        T acc[VEC];
+#pragma unroll
+        for (int c = 0; c < VEC; ++c) acc[c] = T(0);
+        if (in && vv < R.nv)
+            for (int64_t it = i0 + slot; it < i1; it += stride) {
+                const Vec<T, VEC> x = ldg_vec<T, VEC>(R.part + it * R.Wp + vv * VEC);
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+            }
+        for (int o = gp / 2; o >= 1; o >>= 1)
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) {
+                const T y = __shfl_down_sync(0xffffffffu, acc[c], o * R.nvs);
+                if (grp < o) acc[c] += y;
+            }
+        if (grp == 0)
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) wsum[warp][vl * VEC + c] = acc[c];
+        __syncthreads();
+        if (warp == 0 && grp == 0 && vv < R.nv) {
+            T tot[VEC];
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) {
+                tot[c] = T(0);
+                for (int w = 0; w < 8; ++w) tot[c] += wsum[w][vl * VEC + c];
+            }
+            if (vec_in_group0<T, VEC>(R, vv)) {
+                const int64_t idx0 = (int64_t)key * R.g0.width + vv * VEC;
+                VecStep<T, VEC> st;
+                st.prefetch(R.g0, idx0, R.opt.kind);
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) tot[c] *= R.inv_bsz;
+                st.commit(R.g0, idx0, tot, R.opt);
+            } else {
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) {
+                    const int col = vv * VEC + c;
+                    if (col < R.W) apply_col(R, key, col, tot[c]);
+                }
+            }
+        }
         __syncthreads();
     }
 }
 
 // ----------------------------------------------------------------- host --
+
+// Phase timing on the training stream, printed to stderr when the
+// environment variable MFM_B200_TIMING is set (diagnostics only).
+struct PhaseTimer {
+    bool on = false;
+    cudaStream_t s = nullptr;
+    cudaEvent_t last = nullptr;
+    std::string report;
+    explicit PhaseTimer(cudaStream_t st) : s(st) {
+        const char* e = getenv("MFM_B200_TIMING");
+        on = e && *e && *e != '0';
+        if (on) {
+            cudaEventCreate(&last);
+            cudaEventRecord(last, s);
+        }
+    }
+    void mark(const char* name) {
+        if (!on) return;
+        cudaEvent_t now;
+        cudaEventCreate(&now);
+        cudaEventRecord(now, s);
+        cudaEventSynchronize(now);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, last, now);
+        cudaEventDestroy(last);
+        last = now;
+        report += fmt(" %s=%.3fms", name, ms);
+    }
+    ~PhaseTimer() {
+        if (!on) return;
+        if (last) cudaEventDestroy(last);
+        fprintf(stderr, "mfm timing:%s\n", report.c_str());
+    }
+};
 
 unsigned blocks_for(int64_t n, int nt) { return (unsigned)std::max<int64_t>(1, ceil_div(n, nt)); }
 
@@ -686,7 +1048,9 @@ template <class T>
 struct Stream {
     int kind = FEAT;
     int64_t n_keys = 0;
-    int W = 0, cb1 = 0;
+    int W = 0, Wp = 0, cb1 = 0;  // used columns, padded row stride, first column of group 1
+    DevBuf<ItemDesc> desc;
+    DevBuf<uint32_t> inv;
     GroupDev<T> g0{}, g1{};
     // per-epoch plan
     DevBuf<int64_t> estart, seg_lo, run_start, item_start, item_run, long_list, bitem, blong;
@@ -843,6 +1207,13 @@ struct Trainer {
         if (Rn > 0)
             items_kernel<<<blocks_for(Rn, 256), 256, 0, s>>>(st_.item_start.ptr, lscan.ptr, Rn,
                                                            st_.item_run.ptr, st_.long_list.ptr);
+        st_.desc.alloc(device, tot[0]);
+        if (tot[0] > 0)
+            desc_kernel<<<blocks_for(tot[0], 256), 256, 0, s>>>(
+                st_.item_run.ptr, st_.item_start.ptr, st_.run_start.ptr, st_.keys, tot[0],
+                st_.desc.ptr);
+        if (st_.inv.n < (size_t)N || !st_.inv.ptr) st_.inv.alloc(device, N);
+        if (N > 0) inverse_kernel<<<(unsigned)nb, 256, 0, s>>>(st_.seg_lo.ptr, st_.vals, st_.inv.ptr);
         st_.bitem.alloc(device, nb + 1);
         st_.blong.alloc(device, nb + 1);
         batch_tables_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(
@@ -857,33 +1228,63 @@ struct Trainer {
         st_.max_items = 0;
         for (int64_t b = 0; b < nb; ++b)
             st_.max_items = std::max(st_.max_items, st_.h_item[b + 1] - st_.h_item[b]);
-        if (st_.pay.n < (size_t)(st_.max_entries * st_.W) || !st_.pay.ptr)
-            st_.pay.alloc(device, std::max<int64_t>(1, st_.max_entries * st_.W));
-        if (st_.part.n < (size_t)(st_.max_items * st_.W) || !st_.part.ptr)
-            st_.part.alloc(device, std::max<int64_t>(1, st_.max_items * st_.W));
+        if (st_.pay.n < (size_t)(st_.max_entries * st_.Wp) || !st_.pay.ptr)
+            st_.pay.alloc(device, std::max<int64_t>(1, st_.max_entries * st_.Wp));
+        if (st_.part.n < (size_t)(st_.max_items * st_.Wp) || !st_.part.ptr)
+            st_.part.alloc(device, std::max<int64_t>(1, st_.max_items * st_.Wp));
     }
 
-    RedArgs<T> red_args(Stream<T>& st_, T inv_bsz) {
+    RedArgs<T> red_args(Stream<T>& st_, int64_t b, T inv_bsz) {
+        constexpr int VEC = 16 / (int)sizeof(T);
         RedArgs<T> R;
-        R.keys = st_.keys;
-        R.vals = st_.vals;
-        R.run_start = st_.run_start.ptr;
+        R.desc = st_.desc.ptr;
         R.item_start = st_.item_start.ptr;
-        R.item_run = st_.item_run.ptr;
         R.long_list = st_.long_list.ptr;
         R.pay = st_.pay.ptr;
         R.part = st_.part.ptr;
         R.W = st_.W;
+        R.Wp = st_.Wp;
         R.cb1 = st_.cb1;
+        R.nv = st_.Wp / VEC;
+        R.nvs = std::min(R.nv, 32);
+        R.gpw = 32 / R.nvs;
+        R.vec0 = st_.g0.width % VEC == 0 ? 1 : 0;
+        R.seg = st_.h_seg[b];
+        R.item0 = st_.h_item[b];
         R.g0 = st_.g0;
         R.g1 = st_.g1;
         R.opt = opt;
         R.inv_bsz = inv_bsz;
+        R.grow = grow.ptr;
+        R.C = C;
+        R.gw0 = G[0];
+        R.do_w0 = 0;
+        R.nrows = 0;
         return R;
     }
 
     void launch_forward(const FwdArgs<T>& A, int64_t nrows) {
         const unsigned grid = warp_grid(device, nrows, 8, 8);
+        if (model == M_FM && !multiclass) {
+            constexpr int VW = 16 / (int)sizeof(T);
+            if (k % VW == 0 && k / VW <= 8) {
+                const int nvec = (int)(k / VW);
+                const unsigned g = (unsigned)sm_count(device) * 8;
+#define MFM_FROWS(L_, LR_, CAP_)                                                            \
+    {                                                                                       \
+        const int64_t want = ceil_div(nrows * LR_, 256);                                    \
+        fm_forward_rows_kernel<T, VW, L_, LR_, CAP_>                                        \
+            <<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(g, want)), 256, 0, s>>>(A); \
+        MFM_CHECK_LAUNCH("FM forward");                                                     \
+        return;                                                                             \
+    }
+                if (nvec <= 1) MFM_FROWS(1, 16, 48)
+                if (nvec <= 2) MFM_FROWS(2, 16, 48)
+                if (nvec <= 4) MFM_FROWS(4, 16, 48)
+                MFM_FROWS(8, 32, 32)
+#undef MFM_FROWS
+            }
+        }
         if (model == M_FM) {
             const int D = C * (int)k;
             int Lc = 1, lgc = 0;
@@ -934,29 +1335,29 @@ struct Trainer {
         MFM_CHECK_LAUNCH("forward");
     }
 
-    void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz) {
+    void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz, int64_t nrows, bool do_w0) {
+        constexpr int VEC = 16 / (int)sizeof(T);
         const int64_t i0 = st_.h_item[b], i1 = st_.h_item[b + 1];
         const int64_t l0 = st_.h_long[b], l1 = st_.h_long[b + 1];
-        RedArgs<T> R = red_args(st_, inv_bsz);
+        RedArgs<T> R = red_args(st_, b, inv_bsz);
         if (i1 > i0) {
-            const unsigned grid = blocks_for(i1 - i0, 8);
-            if (st_.W <= 32)
-                reduce_stage1_kernel<T, 1><<<grid, 256, 0, s>>>(R, i0, i1);
-            else if (st_.W <= 64)
-                reduce_stage1_kernel<T, 2><<<grid, 256, 0, s>>>(R, i0, i1);
-            else
-                reduce_stage1_kernel<T, 4><<<grid, 256, 0, s>>>(R, i0, i1);
+            const int64_t warps = ceil_div(i1 - i0, R.gpw);
+            reduce_items_kernel<T, VEC><<<blocks_for(warps, 8), 256, 0, s>>>(R, i1 - i0);
             MFM_CHECK_LAUNCH("reduce stage 1");
         }
-        if (l1 > l0) {
-            reduce_stage2_kernel<T><<<blocks_for(l1 - l0, 8), 256, 0, s>>>(R, l0, l1, i0);
+        R.do_w0 = do_w0 ? 1 : 0;
+        R.nrows = nrows;
+        if (l1 > l0 || do_w0) {
+            const unsigned blocks = (unsigned)(l1 - l0) + 1;
+            reduce_runs_kernel<T, VEC><<<blocks, 256, 0, s>>>(R, l0, l1 - l0);
             MFM_CHECK_LAUNCH("reduce stage 2");
         }
     }
 
-    void run(const FwdArgs<T>& base) {
+    void run(const FwdArgs<T>& base, PhaseTimer& pt) {
         for (int64_t e = 0; e < E; ++e) {
             for (int si = 0; si < n_streams; ++si) plan(S[si], (int)e);
+            pt.mark("plan");
             for (int64_t b = 0; b < nb; ++b) {
                 const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                 const T inv_bsz = T(1) / (T)nrows;  // divide by batch length (fm.rs:395-398)
@@ -967,18 +1368,20 @@ struct Trainer {
                 A.estart1 = S[0].estart.ptr;
                 A.seg1 = S[0].h_seg[b];
                 A.pay1 = S[0].pay.ptr;
-                A.W1 = S[0].W;
+                A.W1 = S[0].Wp;
+                A.inv1 = S[0].inv.ptr;
                 if (n_streams > 1) {
                     A.estart2 = S[1].estart.ptr;
                     A.seg2 = S[1].h_seg[b];
                     A.pay2 = S[1].pay.ptr;
-                    A.W2 = S[1].W;
+                    A.W2 = S[1].Wp;
+                    A.inv2 = S[1].inv.ptr;
                 }
                 launch_forward(A, nrows);
-                for (int si = 0; si < n_streams; ++si) launch_reduce(S[si], b, inv_bsz);
-                w0_kernel<T><<<1, 256, 0, s>>>(grow.ptr, nrows, C, G[0], opt, inv_bsz);
-                MFM_CHECK_LAUNCH("w0 step");
+                for (int si = 0; si < n_streams; ++si)
+                    launch_reduce(S[si], b, inv_bsz, nrows, si == n_streams - 1);
             }
+            pt.mark("batches");
         }
         MFM_CUDA(cudaStreamSynchronize(s), "training");
     }
@@ -1047,6 +1450,7 @@ void fit_impl(const FitSpec& f, int device) {
     tr.device = device;
     tr.s = device_stream(device);
     cudaStream_t s = tr.s;
+    PhaseTimer pt(s);
     tr.model = f.model;
     tr.C = (int)f.C;
     tr.multiclass = f.multiclass;
@@ -1122,39 +1526,41 @@ void fit_impl(const FitSpec& f, int device) {
                     c->ftrl_beta, {c->l1_linear, c->l1_factors, 0.0},
                     {c->l2_linear, c->l2_factors, 0.0}};
 
-    // entry streams
+    // entry streams; payload columns are [V part | w part] so that the latent
+    // columns start on a 16-byte boundary
     const int C = tr.C;
+    constexpr int VW = 16 / (int)sizeof(T);
     Stream<T>& s0 = tr.S[0];
     s0.kind = FEAT;
     s0.n_keys = nf;
-    s0.g0 = tr.G[1];
     if (f.model == M_FFM) {
-        s0.W = C;
+        s0.W = C;  // w only
         s0.cb1 = C;
-        s0.g1 = tr.G[1];
+        s0.g0 = s0.g1 = tr.G[1];
         Stream<T>& s1 = tr.S[1];
         s1.kind = SLOT;
         s1.n_keys = nf * F;
         s1.W = (int)(C * k);
         s1.cb1 = s1.W;
-        s1.g0 = tr.G[2];
-        s1.g1 = tr.G[2];
+        s1.g0 = s1.g1 = tr.G[2];
         tr.n_streams = 2;
     } else {
-        s0.W = (int)(C + C * k);
-        s0.cb1 = C;
-        s0.g1 = tr.G[2];
+        s0.W = (int)(C * k + C);  // [V (C*k) | w (C)]
+        s0.cb1 = (int)(C * k);
+        s0.g0 = tr.G[2];
+        s0.g1 = tr.G[1];
         if (f.model == M_FWFM) {
             Stream<T>& s1 = tr.S[1];
             s1.kind = PAIR;
             s1.n_keys = F * F;
             s1.W = C;
             s1.cb1 = C;
-            s1.g0 = tr.G[3];
-            s1.g1 = tr.G[3];
+            s1.g0 = s1.g1 = tr.G[3];
             tr.n_streams = 2;
         }
     }
+    for (int si = 0; si < tr.n_streams; ++si)
+        tr.S[si].Wp = (int)ceil_div(tr.S[si].W, VW) * VW;
     tr.grow.alloc(device, std::max<int64_t>(1, std::min(tr.B, n)) * C);
 
     FwdArgs<T> A{};
@@ -1177,7 +1583,8 @@ void fit_impl(const FitSpec& f, int device) {
     A.r = tr.par[3].ptr;
     A.fid = tr.fid.ptr;
     A.grow = tr.grow.ptr;
-    if (n > 0) tr.run(A);
+    pt.mark("upload");
+    if (n > 0) tr.run(A, pt);
 
     tr.download_group(0, f.w0, 1, 1);
     tr.download_group(1, f.w, nf, 1);
@@ -1186,6 +1593,7 @@ void fit_impl(const FitSpec& f, int device) {
     else
         tr.download_group(2, f.v, nf, k);
     if (f.model == M_FWFM) tr.download_group(3, f.r, F * F, 1);
+    pt.mark("download");
 }
 
 void fit_dispatch(const FitSpec& f, const mfm_exec* ex) {
