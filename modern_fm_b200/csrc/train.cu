@@ -438,16 +438,14 @@ __device__ __forceinline__ void row_gradients(const FwdArgs<T>& A, int64_t row, 
 // lane. Payload per nonzero: [g_c (x cache_cf - v_cf x^2) (C*k) | g_c x (C)]
 // (FmGradAccum::add_row, rust/src/fm.rs:133-146).
 template <class T, int MCOL>
-__global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) {
-    extern __shared__ unsigned char smraw[];
+__device__ __forceinline__ void fm_forward_dev(const FwdArgs<T>& A, int lgc, unsigned char* smraw,
+                                               int64_t warp0, int64_t nwarps) {
     const int C = A.C, k = A.k, D = C * k;
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     T* sm = reinterpret_cast<T*>(smraw) + (size_t)wib * (D + 3 * C);
     T *colv = sm, *lins = sm + D, *logit = lins + C, *gs = logit + C;
     const int Lc = 1 << lgc, G = 32 >> lgc, grp = lane >> lgc, l = lane & (Lc - 1);
-    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
-         j += nwarps) {
+    for (int64_t j = warp0; j < A.nrows; j += nwarps) {
         const int64_t pos = A.pos0 + j, row = A.order[pos];
         const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
         T cache[MCOL], sq[MCOL];
@@ -537,6 +535,13 @@ __global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) 
     }
 }
 
+template <class T, int MCOL>
+__global__ void __launch_bounds__(256) fm_forward_kernel(FwdArgs<T> A, int lgc) {
+    extern __shared__ unsigned char smraw[];
+    fm_forward_dev<T, MCOL>(A, lgc, smraw, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5,
+                            ((int64_t)gridDim.x * blockDim.x) >> 5);
+}
+
 // Binary FM, latent rows of up to 8 vectors (k <= 32 float32, k <= 16
 // float64): LR lanes per row, L lanes per nonzero (VEC-wide loads), CAP
 // nonzeros per iteration with every gather issued before use (as in the
@@ -611,12 +616,12 @@ __device__ __forceinline__ void rows_payload(const FwdArgs<T>& A, int64_t e0, in
 }
 
 template <class T, int VEC, int L, int LR, int CAP>
-__global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
+__device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t slot0,
+                                                    int64_t nslots) {
     using Sh = RowsShape<T, VEC, L, LR, CAP>;
     const int lane = threadIdx.x & 31, rl = lane & (LR - 1), grp = rl / L, l = rl % L;
     const bool act = l < A.k / VEC;
-    const int64_t nslots = ((int64_t)gridDim.x * blockDim.x) / LR;
-    for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR;; j += nslots) {
+    for (int64_t j = slot0;; j += nslots) {
         const bool live = j < A.nrows;
         if (!__any_sync(0xffffffffu, live)) break;
         const int64_t pos = A.pos0 + j;
@@ -675,6 +680,13 @@ __global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
             }
         }
     }
+}
+
+template <class T, int VEC, int L, int LR, int CAP>
+__global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
+    fm_forward_rows_dev<T, VEC, L, LR, CAP>(
+        A, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR,
+        ((int64_t)gridDim.x * blockDim.x) / LR);
 }
 
 // FFM (binary and multiclass). Device V layout (n, F, C, k).
@@ -876,10 +888,12 @@ __device__ __forceinline__ bool vec_in_group0(const RedArgs<T>& R, int vv) {
 // group; each lane sums VEC-wide column vectors over the item's contiguous
 // payload rows. Items of single-item runs apply the optimizer directly.
 template <class T, int VEC>
-__global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t n_items) {
+__device__ __forceinline__ void reduce_items_dev(const RedArgs<T>& R, int64_t n_items,
+                                                 int64_t warp0, int64_t nwarps) {
     const int lane = threadIdx.x & 31, grp = lane / R.nvs, vl = lane % R.nvs;
     if (grp >= R.gpw) return;
-    const int64_t it = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * R.gpw + grp;
+    for (int64_t wi = warp0;; wi += nwarps) {
+    const int64_t it = wi * R.gpw + grp;
     if (it >= n_items) return;
     const ItemDesc d = R.desc[R.item0 + it];
     const int cnt = (int)(d.cnt & ~kMultiItem);
@@ -916,87 +930,205 @@ __global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t
             }
         }
     }
+    }
+}
+
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t n_items) {
+    reduce_items_dev<T, VEC>(R, n_items, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5,
+                             ((int64_t)gridDim.x * blockDim.x) >> 5);
 }
 
 // Stage 2: one block per multi-item run. 8 warps x gp lane groups take the
 // run's item partials in a fixed stride, a shuffle tree folds the groups of a
 // warp and shared memory folds the warps in order, then the run is applied.
 // The last block steps w0 from the batch's per-row gradients (fixed tree).
-template <class T, int VEC>
-__global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t l0, int64_t n_long) {
-    __shared__ T sm[256];
-    __shared__ __align__(16) T wsum[8][32 * VEC];
-    if (blockIdx.x == gridDim.x - 1) {
-        if (!R.do_w0) return;
-        for (int c = 0; c < R.C; ++c) {
-            T s = T(0);
-            for (int64_t j = threadIdx.x; j < R.nrows; j += 256) s += R.grow[j * R.C + c];
-            sm[threadIdx.x] = s;
-            __syncthreads();
-            for (int h = 128; h > 0; h >>= 1) {
-                if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
-                __syncthreads();
-            }
-            if (threadIdx.x == 0) opt_step(R.gw0, c, sm[0] * R.inv_bsz, R.opt);
+// w0: the batch's per-row gradients summed in a fixed tree by one block,
+// then one step per class (step_param with l1 = l2 = 0, optimizer.rs:114-135).
+template <class T>
+__device__ __forceinline__ void w0_dev(const RedArgs<T>& R, T* sm) {
+    for (int c = 0; c < R.C; ++c) {
+        T s = T(0);
+        for (int64_t j = threadIdx.x; j < R.nrows; j += blockDim.x) s += R.grow[j * R.C + c];
+        sm[threadIdx.x] = s;
+        __syncthreads();
+        for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+            if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
             __syncthreads();
         }
-        return;
+        if (threadIdx.x == 0) opt_step(R.gw0, c, sm[0] * R.inv_bsz, R.opt);
+        __syncthreads();
     }
-    const int64_t li = blockIdx.x;
-    if (li >= n_long) return;  // uniform per block
+}
+
+template <class T, int VEC>
+__device__ __forceinline__ void reduce_runs_dev(const RedArgs<T>& R, int64_t l0, int64_t n_long,
+                                                int64_t blk0, int64_t nblk, T (*wsum)[32 * VEC]) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int64_t r = R.long_list[l0 + li];
-    const int64_t i0 = R.item_start[r] - R.item0, i1 = R.item_start[r + 1] - R.item0;
-    const uint32_t key = R.desc[R.item0 + i0].key;
     int gp = 1;  // power-of-two group count per warp for the shuffle fold
     while (gp * 2 * R.nvs <= 32) gp *= 2;
     const int grp = lane / R.nvs, vl = lane % R.nvs;
     const bool in = grp < gp;
     const int stride = gp * 8, slot = warp * gp + grp;
-    for (int vb = 0; vb < R.nv; vb += R.nvs) {
-        const int vv = vb + vl;
-        T acc[VEC];
+    for (int64_t li = blk0; li < n_long; li += nblk) {  // uniform per block
+        const int64_t r = R.long_list[l0 + li];
+        const int64_t i0 = R.item_start[r] - R.item0, i1 = R.item_start[r + 1] - R.item0;
+        const uint32_t key = R.desc[R.item0 + i0].key;
+        for (int vb = 0; vb < R.nv; vb += R.nvs) {
+            const int vv = vb + vl;
+            T acc[VEC];
 #pragma unroll
-        for (int c = 0; c < VEC; ++c) acc[c] = T(0);
-        if (in && vv < R.nv)
-            for (int64_t it = i0 + slot; it < i1; it += stride) {
-                const Vec<T, VEC> x = ldg_vec<T, VEC>(R.part + it * R.Wp + vv * VEC);
+            for (int c = 0; c < VEC; ++c) acc[c] = T(0);
+            if (in && vv < R.nv)
+                for (int64_t it = i0 + slot; it < i1; it += stride) {
+                    const Vec<T, VEC> x = ldg_vec<T, VEC>(R.part + it * R.Wp + vv * VEC);
 #pragma unroll
-                for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
-            }
-        for (int o = gp / 2; o >= 1; o >>= 1)
-#pragma unroll
-            for (int c = 0; c < VEC; ++c) {
-                const T y = __shfl_down_sync(0xffffffffu, acc[c], o * R.nvs);
-                if (grp < o) acc[c] += y;
-            }
-        if (grp == 0)
-#pragma unroll
-            for (int c = 0; c < VEC; ++c) wsum[warp][vl * VEC + c] = acc[c];
-        __syncthreads();
-        if (warp == 0 && grp == 0 && vv < R.nv) {
-            T tot[VEC];
-#pragma unroll
-            for (int c = 0; c < VEC; ++c) {
-                tot[c] = T(0);
-                for (int w = 0; w < 8; ++w) tot[c] += wsum[w][vl * VEC + c];
-            }
-            if (vec_in_group0<T, VEC>(R, vv)) {
-                const int64_t idx0 = (int64_t)key * R.g0.width + vv * VEC;
-                VecStep<T, VEC> st;
-                st.prefetch(R.g0, idx0, R.opt.kind);
-#pragma unroll
-                for (int c = 0; c < VEC; ++c) tot[c] *= R.inv_bsz;
-                st.commit(R.g0, idx0, tot, R.opt);
-            } else {
+                    for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+                }
+            for (int o = gp / 2; o >= 1; o >>= 1)
 #pragma unroll
                 for (int c = 0; c < VEC; ++c) {
-                    const int col = vv * VEC + c;
-                    if (col < R.W) apply_col(R, key, col, tot[c]);
+                    const T y = __shfl_down_sync(0xffffffffu, acc[c], o * R.nvs);
+                    if (grp < o) acc[c] += y;
+                }
+            if (grp == 0)
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) wsum[warp][vl * VEC + c] = acc[c];
+            __syncthreads();
+            if (warp == 0 && grp == 0 && vv < R.nv) {
+                T tot[VEC];
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) {
+                    tot[c] = T(0);
+                    for (int w = 0; w < 8; ++w) tot[c] += wsum[w][vl * VEC + c];
+                }
+                if (vec_in_group0<T, VEC>(R, vv)) {
+                    const int64_t idx0 = (int64_t)key * R.g0.width + vv * VEC;
+                    VecStep<T, VEC> st;
+                    st.prefetch(R.g0, idx0, R.opt.kind);
+#pragma unroll
+                    for (int c = 0; c < VEC; ++c) tot[c] *= R.inv_bsz;
+                    st.commit(R.g0, idx0, tot, R.opt);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < VEC; ++c) {
+                        const int col = vv * VEC + c;
+                        if (col < R.W) apply_col(R, key, col, tot[c]);
+                    }
                 }
             }
+            __syncthreads();
         }
-        __syncthreads();
+    }
+}
+
+// Stage 2 as its own launch: one block per multi-item run; the last block
+// steps w0.
+template <class T, int VEC>
+__global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t l0, int64_t n_long) {
+    __shared__ T sm[256];
+    __shared__ __align__(16) T wsum[8][32 * VEC];
+    if (blockIdx.x == gridDim.x - 1) {
+        if (R.do_w0) w0_dev(R, sm);
+        return;
+    }
+    reduce_runs_dev<T, VEC>(R, l0, n_long, blockIdx.x, gridDim.x - 1, wsum);
+}
+
+// --------------------------------------------------- persistent epoch loop --
+//
+// FM training runs a whole epoch's batch loop in one cooperative launch (all
+// blocks co-resident): forward -> barrier -> stage 1 (+ w0 by block 0) ->
+// [barrier -> stage 2, when the batch has multi-item runs] -> barrier. The
+// grid barrier's wait is bounded: after kBarrierSpinLimit polls it records an
+// error and moves on, so the launch always ends and the host reports
+// MFM_ERR_DEVICE_CHECK instead of waiting forever.
+
+struct GridBar {
+    unsigned int count, gen, err, pad;
+};
+constexpr unsigned long long kBarrierSpinLimit = 1ull << 24;  // polls of ~100 ns
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void grid_barrier(GridBar* bar, unsigned int& gen) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int g = gen;
+        __threadfence();  // release this block's writes
+        const unsigned int arrived = atomicAdd(&bar->count, 1u);
+        if (arrived == gridDim.x - 1) {
+            atomicExch(&bar->count, 0u);
+            __threadfence();
+            atomicExch(&bar->gen, g + 1u);
+        } else {
+            unsigned long long polls = 0;
+            while (ld_acquire_gpu(&bar->gen) == g) {
+                if (++polls > kBarrierSpinLimit) {
+                    atomicOr(&bar->err, 1u);
+                    break;
+                }
+                __nanosleep(100);
+            }
+        }
+        __threadfence();  // acquire the other blocks' writes
+    }
+    ++gen;
+    __syncthreads();
+}
+
+template <class T>
+struct EpochArgs {
+    FwdArgs<T> fwd;  // per-batch fields are filled in the loop
+    RedArgs<T> red;
+    const int64_t* seg_lo;  // per-batch entry starts (nb + 1)
+    const int64_t* bitem;   // per-batch first work item (nb + 1)
+    const int64_t* blong;   // per-batch first multi-item run (nb + 1)
+    int64_t nb, B, n_rows;
+    GridBar* bar;
+};
+
+// FK = 0: row-group forward <L = P1, LR = P2, CAP = P3>; FK = 1: generic
+// forward with MCOL = P1 (multiclass and other widths).
+template <class T, int VEC, int FK, int P1, int P2, int P3>
+__global__ void __launch_bounds__(256, 2) fm_epoch_kernel(EpochArgs<T> E, int lgc) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    T* sm = reinterpret_cast<T*>(smraw);
+    T(*wsum)[32 * VEC] = reinterpret_cast<T(*)[32 * VEC]>(sm + 256);
+    unsigned char* fwd_smem = reinterpret_cast<unsigned char*>(sm + 256 + 8 * 32 * VEC);
+    unsigned int gen = 0;
+    const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t b = 0; b < E.nb; ++b) {
+        const int64_t pos0 = b * E.B;
+        const int64_t nrows = E.n_rows - pos0 < E.B ? E.n_rows - pos0 : E.B;
+        FwdArgs<T> A = E.fwd;
+        A.pos0 = pos0;
+        A.nrows = nrows;
+        A.seg1 = E.seg_lo[b];
+        if constexpr (FK == 0)
+            fm_forward_rows_dev<T, VEC, P1, P2, P3>(A, gtid / P2, nthreads / P2);
+        else
+            fm_forward_dev<T, P1>(A, lgc, fwd_smem, gtid >> 5, nthreads >> 5);
+        grid_barrier(E.bar, gen);
+        RedArgs<T> R = E.red;
+        R.seg = A.seg1;
+        R.item0 = E.bitem[b];
+        R.nrows = nrows;
+        R.inv_bsz = T(1) / (T)nrows;
+        const int64_t n_items = E.bitem[b + 1] - R.item0;
+        const int64_t l0 = E.blong[b], nl = E.blong[b + 1] - l0;
+        if (blockIdx.x == 0) w0_dev(R, sm);
+        reduce_items_dev<T, VEC>(R, n_items, gtid >> 5, nthreads >> 5);
+        if (nl > 0) {
+            grid_barrier(E.bar, gen);
+            reduce_runs_dev<T, VEC>(R, l0, nl, blockIdx.x, gridDim.x, wsum);
+        }
+        grid_barrier(E.bar, gen);
     }
 }
 
@@ -1080,6 +1212,8 @@ struct Trainer {
     OptDev opt;
     Stream<T> S[2];
     int n_streams = 1;
+    DevBuf<GridBar> bar;
+    bool coop = false;  // cooperative launches usable (persistent epoch loop)
 
     void upload_group(int gi, const mfm_group* hg, int64_t R, int64_t K, int reg) {
         const int64_t n = (int64_t)C * R * K;
@@ -1354,10 +1488,88 @@ struct Trainer {
         }
     }
 
+    // Cooperative launch of fm_epoch_kernel over all co-resident blocks.
+    template <int FK, int P1, int P2, int P3>
+    void launch_epoch_t(const FwdArgs<T>& base, int lgc, size_t fwd_smem) {
+        constexpr int VEC = 16 / (int)sizeof(T);
+        auto kern = fm_epoch_kernel<T, VEC, FK, P1, P2, P3>;
+        const size_t smem = (256 + 8 * 32 * VEC) * sizeof(T) + fwd_smem;
+        if (smem > 48 * 1024)
+            MFM_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem),
+                     "epoch kernel smem attribute");
+        int per_sm = 0;
+        MFM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem),
+                 "epoch kernel occupancy");
+        if (per_sm < 1) fail(MFM_ERR_UNSUPPORTED, "epoch kernel does not fit on an SM");
+        EpochArgs<T> EA;
+        EA.fwd = base;
+        EA.red = red_args(S[0], 0, T(1));
+        EA.seg_lo = S[0].seg_lo.ptr;
+        EA.bitem = S[0].bitem.ptr;
+        EA.blong = S[0].blong.ptr;
+        EA.nb = nb;
+        EA.B = B;
+        EA.n_rows = n_rows;
+        EA.bar = bar.ptr;
+        MFM_CUDA(cudaMemsetAsync(bar.ptr, 0, sizeof(GridBar), s), "barrier init");
+        void* args[] = {&EA, &lgc};
+        MFM_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(per_sm * sm_count(device)),
+                                             dim3(256), args, smem, s),
+                 "epoch kernel launch");
+        GridBar h{};
+        d2h(&h, bar.ptr, 1, s, "barrier status");
+        MFM_CUDA(cudaStreamSynchronize(s), "epoch kernel");
+        if (h.err)
+            fail(MFM_ERR_DEVICE_CHECK,
+                 "a grid barrier wait gave up (blocks were not co-resident); results invalid");
+    }
+
+    // true when the whole epoch ran as one persistent launch
+    bool launch_epoch(const FwdArgs<T>& base) {
+        if (model != M_FM || n_streams != 1 || !coop) return false;
+        constexpr int VW = 16 / (int)sizeof(T);
+        if (!multiclass && k % VW == 0 && k / VW <= 8) {
+            const int nvec = (int)(k / VW);
+            if (nvec <= 1) launch_epoch_t<0, 1, 16, 48>(base, 0, 0);
+            else if (nvec <= 2) launch_epoch_t<0, 2, 16, 48>(base, 0, 0);
+            else if (nvec <= 4) launch_epoch_t<0, 4, 16, 48>(base, 0, 0);
+            else launch_epoch_t<0, 8, 32, 32>(base, 0, 0);
+            return true;
+        }
+        const int D = C * (int)k;
+        int Lc = 1, lgc = 0;
+        while (Lc < D && Lc < 32) {
+            Lc <<= 1;
+            ++lgc;
+        }
+        const int mcol = (D + Lc - 1) / Lc;
+        const size_t fs = (size_t)8 * (D + 3 * C) * sizeof(T);
+        if (mcol <= 1) launch_epoch_t<1, 1, 0, 0>(base, lgc, fs);
+        else if (mcol <= 2) launch_epoch_t<1, 2, 0, 0>(base, lgc, fs);
+        else if (mcol <= 4) launch_epoch_t<1, 4, 0, 0>(base, lgc, fs);
+        else if (mcol <= 8) launch_epoch_t<1, 8, 0, 0>(base, lgc, fs);
+        else if (mcol <= 16) launch_epoch_t<1, 16, 0, 0>(base, lgc, fs);
+        else launch_epoch_t<1, 32, 0, 0>(base, lgc, fs);
+        return true;
+    }
+
     void run(const FwdArgs<T>& base, PhaseTimer& pt) {
         for (int64_t e = 0; e < E; ++e) {
             for (int si = 0; si < n_streams; ++si) plan(S[si], (int)e);
             pt.mark("plan");
+            {
+                FwdArgs<T> A = base;
+                A.order = order_all.ptr + e * n_rows;
+                A.estart1 = S[0].estart.ptr;
+                A.pay1 = S[0].pay.ptr;
+                A.W1 = S[0].Wp;
+                A.inv1 = S[0].inv.ptr;
+                if (launch_epoch(A)) {
+                    pt.mark("batches");
+                    continue;
+                }
+            }
             for (int64_t b = 0; b < nb; ++b) {
                 const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                 const T inv_bsz = T(1) / (T)nrows;  // divide by batch length (fm.rs:395-398)
@@ -1561,6 +1773,15 @@ void fit_impl(const FitSpec& f, int device) {
     }
     for (int si = 0; si < tr.n_streams; ++si)
         tr.S[si].Wp = (int)ceil_div(tr.S[si].W, VW) * VW;
+    {
+        int co = 0;
+        MFM_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, device), "attribute");
+        // The persistent epoch loop (one cooperative launch per epoch) is opt-in:
+        // at 4096-row batches the per-batch launches are faster today.
+        const char* pe = getenv("MFM_B200_EPOCH_KERNEL");
+        tr.coop = co != 0 && pe && *pe == '1';
+        tr.bar.alloc(device, 1);
+    }
     tr.grow.alloc(device, std::max<int64_t>(1, std::min(tr.B, n)) * C);
 
     FwdArgs<T> A{};
