@@ -196,6 +196,156 @@ def make_params(local, dev_t):
     return -3.0, w, V
 
 
+TRAIN_ROWS = 10_000_000
+TRAIN_BATCH = 4096
+
+
+def train_measure(args, rank, world, local, dev_t, L, _lib):
+    """FM AdaGrad training on the large CTR config: 10M rows, batch 4096,
+    k=16, float32, one epoch per step. Returns the `train` object of the
+    JSON line (rank 0) or None."""
+    import torch
+
+    from modern_fm_b200 import workloads as WL
+
+    n = args.train_rows
+    X = WL.ctr_fm_torch(n, SEED + 100 + rank, device=dev_t)
+    g = torch.Generator(device=dev_t)
+    g.manual_seed(4321 + rank)
+    # labels from a planted FM with N(0, 0.1) parameters at ~3 % positives
+    wp = (torch.randn(N_FEATURES, generator=g, device=dev_t) * 0.1).contiguous()
+    Vp = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.1).contiguous()
+    sc = torch.empty(n, dtype=torch.float32, device=dev_t)
+    stream = torch.cuda.current_stream(dev_t)
+    rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32, local, X["indptr"].data_ptr(),
+                                 X["indices"].data_ptr(), X["data"].data_ptr(), n, 0.0,
+                                 wp.data_ptr(), Vp.data_ptr(), K, sc.data_ptr(), stream.cuda_stream)
+    if rc:
+        raise RuntimeError(_lib.last_error())
+    lo, hi = -50.0, 50.0
+    for _ in range(60):
+        mid = 0.5 * (lo + hi)
+        if float(torch.sigmoid(sc.double() + mid).mean()) > 0.03:
+            hi = mid
+        else:
+            lo = mid
+    y = (torch.rand(n, generator=g, device=dev_t) < torch.sigmoid(sc + 0.5 * (lo + hi))).float()
+    sw = torch.ones(n, device=dev_t)
+    order = torch.randperm(n, generator=g, device=dev_t).to(torch.int32).contiguous()
+    # algorithmic bytes of one epoch: per row the scoring gathers (2976 B) + y,
+    # sample weight; per (batch, touched feature) param and AdaGrad state read
+    # and written: 4 x (k+1) x 4 B
+    rows_of = torch.repeat_interleave(
+        torch.arange(n, device=dev_t), X["indptr"][1:] - X["indptr"][:-1])
+    pos_of = torch.empty(n, dtype=torch.int64, device=dev_t)
+    pos_of[order.long()] = torch.arange(n, device=dev_t)
+    keys = (pos_of[rows_of] // TRAIN_BATCH) * N_FEATURES + X["indices"].long()
+    touched = int(torch.unique(keys).numel())
+    del rows_of, pos_of, keys
+    bytes_epoch = n * (BYTES_PER_ROW - 4 + 8) + touched * (K + 1) * 4 * 4
+
+    w0 = torch.zeros(1, device=dev_t)
+    w = torch.zeros(N_FEATURES, device=dev_t)
+    V = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.01).contiguous()
+    acc0, accw, accV = torch.zeros(1, device=dev_t), torch.zeros_like(w), torch.zeros_like(V)
+    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
+                    1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, None, 1, TRAIN_BATCH)
+    grp = [_lib.DevGroup(p.data_ptr(), a.data_ptr(), None, None, None, None, None)
+           for p, a in ((w0, acc0), (w, accw), (V, accV))]
+
+    def epoch():
+        rc = L.mfm_fm_fit_device(_lib.MFM_DTYPE_F32, local, X["indptr"].data_ptr(),
+                                 X["indices"].data_ptr(), X["data"].data_ptr(), n, N_FEATURES,
+                                 y.data_ptr(), sw.data_ptr(), order.data_ptr(), tr, K, grp[0],
+                                 grp[1], grp[2], stream.cuda_stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    epoch()  # warm-up: allocator and module load
+    torch.cuda.synchronize()
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.train_steps):
+        epoch()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.train_steps, world)
+    if not np.isfinite(float(V.abs().max())):
+        raise RuntimeError("training diverged")
+
+    # e2e: the reference-facing fit entry point with pinned host buffers in
+    # the boundary format (int64 indices, float64 values / parameters / state)
+    n_e = min(n, args.train_e2e_rows)
+    ip = X["indptr"][: n_e + 1].cpu().pin_memory()
+    ix = X["indices"][: int(ip[-1])].to(torch.int64).cpu().pin_memory()
+    dv = X["data"][: int(ip[-1])].to(torch.float64).cpu().pin_memory()
+    yh = y[:n_e].double().cpu().pin_memory()
+    swh = torch.ones(n_e, dtype=torch.float64).pin_memory()
+    roh = torch.arange(n_e, dtype=torch.int64).reshape(1, -1).pin_memory()
+    wh = torch.zeros(N_FEATURES, dtype=torch.float64).pin_memory()
+    Vh = V.double().cpu().pin_memory()
+    awh, aVh = torch.zeros_like(wh).pin_memory(), torch.zeros_like(Vh).pin_memory()
+    csr, keep = _lib.make_csr(ip.numpy(), ix.numpy(), dv.numpy(), N_FEATURES)
+    tr_h = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
+                      1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, _lib.ptr(roh.numpy(), _lib.i64p), 1,
+                      TRAIN_BATCH)
+    w0a, a0a = np.zeros(1), np.zeros(1)
+    gh = [_lib.Group(_lib.ptr(p), _lib.ptr(a), None, None, None, None, None)
+          for p, a in ((w0a, a0a), (wh.numpy(), awh.numpy()), (Vh.numpy(), aVh.numpy()))]
+    ex = _lib.Exec(_lib.MFM_DTYPE_F32, local, 1)
+
+    def e2e_fit():
+        rc = L.mfm_fm_fit_csr(csr, _lib.ptr(yh.numpy()), _lib.ptr(swh.numpy()), tr_h, K, gh[0],
+                              gh[1], gh[2], ex)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    e2e_fit()
+    barrier(world)
+    t = time.perf_counter()
+    e2e_fit()
+    e2e_s = max_over_ranks(time.perf_counter() - t, world)
+    h2d = sum(a.numpy().nbytes for a in (ip, ix, dv, yh, swh, roh, wh, Vh, awh, aVh)) + 16
+    d2h = sum(a.numpy().nbytes for a in (wh, Vh, awh, aVh)) + 16
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import oracle as O
+
+        n_c = args.train_cpu_rows
+        ipc = ip.numpy()[: n_c + 1]
+        nzc = int(ipc[-1])
+        threads = os.cpu_count() or 1
+        wc, Vc = np.zeros(N_FEATURES), V.double().cpu().numpy()
+        t = time.perf_counter()
+        O.fm_fit_csr(ipc, ix.numpy()[:nzc], dv.numpy()[:nzc], N_FEATURES, yh.numpy()[:n_c],
+                     np.ones(n_c), 0.0, 0.0, wc, Vc, np.zeros(N_FEATURES), np.zeros_like(Vc),
+                     "logistic", "adagrad", 0.05, 1e-5, 1e-5, 0.9, 0.999, 1e-8,
+                     np.arange(n_c)[None, :], TRAIN_BATCH, threads, 0.0, 0.0, 1.0)
+        cpu = {"value": n_c / (time.perf_counter() - t), "unit": "rows/s", "cores": threads,
+               "kind": "port", "sample": f"first {n_c} rows, one epoch, n_jobs={threads} "
+                                         "(contiguous-chunk split, rust/src/fm.rs:286-311)"}
+    if rank != 0:
+        return None
+    peak, _ = peaks()
+    achieved = bytes_epoch / (ms / 1e3) / 1e9
+    out = {
+        "metric": "FM AdaGrad training rows/s (CTR-shaped 39 fields, 2^22 features, k=16, "
+                  "batch 4096, 1 epoch per step)",
+        "value": world * n / (ms / 1e3), "unit": "rows/s", "rows_per_gpu": n,
+        "steps": args.train_steps, "ms_per_step": ms, "scaling": "weak (independent fits)",
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "bytes_per_epoch": bytes_epoch,
+                     "touched_per_epoch": touched},
+        "e2e": {"value": world * n_e / e2e_s, "unit": "rows/s", "rows": n_e,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+    }
+    if cpu:
+        out["cpu_baseline"] = cpu
+    return out
+
+
 def run_ours(args):
     import torch
 
@@ -287,7 +437,7 @@ def run_ours(args):
     e2e_par = bool(np.allclose(out_h.numpy()[:4000], want, rtol=1e-5, atol=1e-5))
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         threads = os.cpu_count() or 1
         n_s = 300_000
         rate, _ = cpu_baseline(Xh, w0, w_h.numpy(), V_h.numpy(), n_s, threads)
@@ -295,6 +445,8 @@ def run_ours(args):
                "sample": f"first {n_s} rows of the rank-0 test batch, rows split over "
                          f"{threads} host threads (the reference's own CPU predict is "
                          "single-threaded, rust/src/fm.rs:58-70)"}
+
+    train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
 
     if rank == 0:
         rows_total = N_ROWS * world
@@ -320,6 +472,8 @@ def run_ours(args):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        if train:
+            line["train"] = train
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -376,6 +530,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--rows", type=int, default=N_ROWS,
                     help="rows per GPU (smaller cases for profiling runs)")
+    ap.add_argument("--no-train", action="store_true", help="skip the training measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS)
+    ap.add_argument("--train-steps", type=int, default=2)
+    ap.add_argument("--train-e2e-rows", type=int, default=2_000_000)
+    ap.add_argument("--train-cpu-rows", type=int, default=200_000)
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the device-resident kernel (profiling runs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])

@@ -210,6 +210,30 @@ int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const double* w, con
 /* Size in bytes of the static array behind mfm_fm_predict_csr_noalloc. */
 int64_t mfm_noalloc_scratch_bytes(void);
 
+/* ---- device-resident training (no reference counterpart) -----------------
+ * Binary FM training over caller-owned DEVICE arrays on `device`: indptr
+ * int64 (n_rows+1), indices int32, data / y / sample_weight / parameters /
+ * state in `dtype`; row_orders int32 (tr->n_epochs, n_rows) on the device
+ * (tr->row_orders is ignored). Hyperparameters, n_epochs and batch_size come
+ * from *tr. Parameters and state are updated in place on the device; a NULL
+ * state pointer means a zeroed state local to the call. The caller guarantees
+ * a canonical, in-range CSR. Runs on `stream` (a cudaStream_t). */
+typedef struct {
+    void* param;
+    void* acc;
+    void* m;
+    void* s;
+    void* t;
+    void* z;
+    void* n;
+} mfm_dev_group;
+
+int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr, const int32_t* indices,
+                      const void* data, int64_t n_rows, int64_t n_features, const void* y,
+                      const void* sample_weight, const int32_t* row_orders,
+                      const mfm_train* tr, int64_t k, mfm_dev_group* w0, mfm_dev_group* w,
+                      mfm_dev_group* v, void* stream);
+
 /* Release the engine's cached device memory on every device. */
 void mfm_release_cached_memory(void);
 

@@ -45,6 +45,11 @@ class Group(ct.Structure):
     _fields_ = [(n, f64p) for n in ("param", "acc", "m", "s", "t", "z", "n")]
 
 
+class DevGroup(ct.Structure):
+    """mfm_dev_group: device pointers (integers) in the compute dtype."""
+    _fields_ = [(n, ct.c_void_p) for n in ("param", "acc", "m", "s", "t", "z", "n")]
+
+
 _SIGNATURES = {
     "mfm_has_cuda": (ct.c_int, []),
     "mfm_last_error": (ct.c_char_p, []),
@@ -73,6 +78,10 @@ _SIGNATURES = {
     "mfm_fwfm_fit_multiclass_csr": (ct.c_int, [ct.POINTER(Csr), i64p, f64p, ct.c_int64, i64p,
                                                ct.c_int64, ct.POINTER(Train), ct.c_int64]
                                     + [ct.POINTER(Group)] * 4 + [ct.POINTER(Exec)]),
+    "mfm_fm_fit_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p, ct.c_void_p,
+                                     ct.c_int64, ct.c_int64, ct.c_void_p, ct.c_void_p,
+                                     ct.c_void_p, ct.POINTER(Train), ct.c_int64]
+                          + [ct.POINTER(DevGroup)] * 3 + [ct.c_void_p]),
     "mfm_fm_predict_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_double, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]),

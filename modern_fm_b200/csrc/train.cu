@@ -1206,9 +1206,15 @@ struct Trainer {
     DevBuf<int64_t> indptr;
     DevBuf<int32_t> indices, order_all, fid, ycls;
     DevBuf<T> data, y, sw, grow;
+    // the device arrays every phase reads: the uploads above, or a caller's
+    // device buffers (mfm_fm_fit_device)
+    const int64_t* p_indptr = nullptr;
+    const int32_t* p_indices = nullptr;
+    const int32_t* p_order = nullptr;
+    const int32_t* p_fid = nullptr;
     // parameters + state per group: 0 = w0, 1 = w, 2 = V, 3 = R
     DevBuf<T> par[4], st[4][6];
-    GroupDev<T> G[4];
+    GroupDev<T> G[4] = {};
     OptDev opt;
     Stream<T> S[2];
     int n_streams = 1;
@@ -1278,10 +1284,10 @@ struct Trainer {
 
     // count -> scan -> expand -> segmented sort -> runs -> items, for epoch e
     void plan(Stream<T>& st_, int e) {
-        const int32_t* order = order_all.ptr + (int64_t)e * n_rows;
+        const int32_t* order = p_order + (int64_t)e * n_rows;
         DevBuf<int64_t> cnt(device, n_rows);
         st_.estart.alloc(device, n_rows + 1);
-        count_kernel<<<blocks_for(n_rows, 256), 256, 0, s>>>(st_.kind, order, indptr.ptr, n_rows,
+        count_kernel<<<blocks_for(n_rows, 256), 256, 0, s>>>(st_.kind, order, p_indptr, n_rows,
                                                            cnt.ptr);
         exclusive_scan<int64_t, int64_t>(device, s, cnt.ptr, n_rows, st_.estart.ptr);
         st_.seg_lo.alloc(device, nb + 1);
@@ -1305,7 +1311,7 @@ struct Trainer {
             st_.v1.alloc(device, N);
         }
         expand_kernel<<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
-            st_.kind, order, indptr.ptr, indices.ptr, fid.ptr, (int)F, n_rows, B,
+            st_.kind, order, p_indptr, p_indices, p_fid, (int)F, n_rows, B,
             st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr);
         MFM_CHECK_LAUNCH("expand");
         SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr,
@@ -1395,6 +1401,101 @@ struct Trainer {
         R.do_w0 = 0;
         R.nrows = 0;
         return R;
+    }
+
+    // Optimizer configuration, entry streams and the forward arguments shared
+    // by every batch. Payload columns are [V part | w part] so that the latent
+    // columns start on a 16-byte boundary.
+    FwdArgs<T> prepare(const mfm_train* c, const T* data, const T* yv, const int32_t* yc,
+                       const T* swv) {
+        opt = OptDev{c->optimizer, c->learning_rate, c->beta_1, c->beta_2, c->epsilon,
+                     c->ftrl_beta, {c->l1_linear, c->l1_factors, 0.0},
+                     {c->l2_linear, c->l2_factors, 0.0}};
+        constexpr int VW = 16 / (int)sizeof(T);
+        Stream<T>& s0 = S[0];
+        s0.kind = FEAT;
+        s0.n_keys = n_feat;
+        if (model == M_FFM) {
+            s0.W = C;  // w only
+            s0.cb1 = C;
+            s0.g0 = s0.g1 = G[1];
+            Stream<T>& s1 = S[1];
+            s1.kind = SLOT;
+            s1.n_keys = n_feat * F;
+            s1.W = (int)(C * k);
+            s1.cb1 = s1.W;
+            s1.g0 = s1.g1 = G[2];
+            n_streams = 2;
+        } else {
+            s0.W = (int)(C * k + C);  // [V (C*k) | w (C)]
+            s0.cb1 = (int)(C * k);
+            s0.g0 = G[2];
+            s0.g1 = G[1];
+            if (model == M_FWFM) {
+                Stream<T>& s1 = S[1];
+                s1.kind = PAIR;
+                s1.n_keys = F * F;
+                s1.W = C;
+                s1.cb1 = C;
+                s1.g0 = s1.g1 = G[3];
+                n_streams = 2;
+            }
+        }
+        for (int si = 0; si < n_streams; ++si) S[si].Wp = (int)ceil_div(S[si].W, VW) * VW;
+        int co = 0;
+        MFM_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, device), "attribute");
+        // The persistent epoch loop (one cooperative launch per epoch) is opt-in:
+        // at 4096-row batches the per-batch launches are faster today.
+        const char* pe = getenv("MFM_B200_EPOCH_KERNEL");
+        coop = co != 0 && pe && *pe == '1';
+        bar.alloc(device, 1);
+        grow.alloc(device, std::max<int64_t>(1, std::min(B, n_rows)) * C);
+        FwdArgs<T> A{};
+        A.indptr = p_indptr;
+        A.indices = p_indices;
+        A.data = data;
+        A.y = yv;
+        A.ycls = yc;
+        A.sw = swv;
+        A.C = C;
+        A.k = (int)k;
+        A.F = (int)F;
+        A.loss = c->loss;
+        A.multiclass = multiclass ? 1 : 0;
+        A.ls_on = (T)(1.0 - c->label_smoothing);
+        A.ls_off = (T)(C > 1 ? c->label_smoothing / ((double)C - 1.0) : 0.0);
+        A.w0 = G[0].p;
+        A.w = G[1].p;
+        A.v = G[2].p;
+        A.r = G[3].p;
+        A.fid = p_fid;
+        A.grow = grow.ptr;
+        return A;
+    }
+
+    // Parameter group `gi` over caller-owned device arrays; missing state
+    // arrays become zeroed buffers local to the call.
+    void device_group(int gi, const mfm_dev_group* dg, int64_t len, int64_t width, int reg) {
+        GroupDev<T>& g = G[gi];
+        g = GroupDev<T>{(T*)dg->param, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                        width, reg};
+        auto st_ptr = [&](int slot, void* ext) -> T* {
+            if (ext) return (T*)ext;
+            st[gi][slot].alloc(device, len);
+            MFM_CUDA(cudaMemsetAsync(st[gi][slot].ptr, 0, len * sizeof(T), s), "state init");
+            return st[gi][slot].ptr;
+        };
+        const int kind = tr->optimizer;
+        if (kind == MFM_OPT_ADAGRAD) g.acc = st_ptr(0, dg->acc);
+        if (kind == MFM_OPT_ADAM) {
+            g.m = st_ptr(1, dg->m);
+            g.s = st_ptr(2, dg->s);
+            g.t = st_ptr(3, dg->t);
+        }
+        if (kind == MFM_OPT_FTRL) {
+            g.z = st_ptr(4, dg->z);
+            g.n = st_ptr(5, dg->n);
+        }
     }
 
     void launch_forward(const FwdArgs<T>& A, int64_t nrows) {
@@ -1560,7 +1661,7 @@ struct Trainer {
             pt.mark("plan");
             {
                 FwdArgs<T> A = base;
-                A.order = order_all.ptr + e * n_rows;
+                A.order = p_order + e * n_rows;
                 A.estart1 = S[0].estart.ptr;
                 A.pay1 = S[0].pay.ptr;
                 A.W1 = S[0].Wp;
@@ -1574,7 +1675,7 @@ struct Trainer {
                 const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                 const T inv_bsz = T(1) / (T)nrows;  // divide by batch length (fm.rs:395-398)
                 FwdArgs<T> A = base;
-                A.order = order_all.ptr + e * n_rows;
+                A.order = p_order + e * n_rows;
                 A.pos0 = pos0;
                 A.nrows = nrows;
                 A.estart1 = S[0].estart.ptr;
@@ -1722,6 +1823,10 @@ void fit_impl(const FitSpec& f, int device) {
         h2d(tr.fid.ptr, f32.data(), nf, s, "field_ids upload");
         MFM_CUDA(cudaStreamSynchronize(s), "field_ids upload");
     }
+    tr.p_indptr = tr.indptr.ptr;
+    tr.p_indices = tr.indices.ptr;
+    tr.p_order = tr.order_all.ptr;
+    tr.p_fid = tr.fid.ptr;
 
     // parameters + optimizer state, device layout (key, class, k)
     const int64_t F = tr.F, k = tr.k;
@@ -1733,79 +1838,10 @@ void fit_impl(const FitSpec& f, int device) {
         tr.upload_group(2, f.v, nf, k, 1);
     if (f.model == M_FWFM) tr.upload_group(3, f.r, F * F, 1, 1);
 
-    const mfm_train* c = f.tr;
-    tr.opt = OptDev{c->optimizer, c->learning_rate, c->beta_1, c->beta_2, c->epsilon,
-                    c->ftrl_beta, {c->l1_linear, c->l1_factors, 0.0},
-                    {c->l2_linear, c->l2_factors, 0.0}};
-
-    // entry streams; payload columns are [V part | w part] so that the latent
-    // columns start on a 16-byte boundary
-    const int C = tr.C;
-    constexpr int VW = 16 / (int)sizeof(T);
-    Stream<T>& s0 = tr.S[0];
-    s0.kind = FEAT;
-    s0.n_keys = nf;
-    if (f.model == M_FFM) {
-        s0.W = C;  // w only
-        s0.cb1 = C;
-        s0.g0 = s0.g1 = tr.G[1];
-        Stream<T>& s1 = tr.S[1];
-        s1.kind = SLOT;
-        s1.n_keys = nf * F;
-        s1.W = (int)(C * k);
-        s1.cb1 = s1.W;
-        s1.g0 = s1.g1 = tr.G[2];
-        tr.n_streams = 2;
-    } else {
-        s0.W = (int)(C * k + C);  // [V (C*k) | w (C)]
-        s0.cb1 = (int)(C * k);
-        s0.g0 = tr.G[2];
-        s0.g1 = tr.G[1];
-        if (f.model == M_FWFM) {
-            Stream<T>& s1 = tr.S[1];
-            s1.kind = PAIR;
-            s1.n_keys = F * F;
-            s1.W = C;
-            s1.cb1 = C;
-            s1.g0 = s1.g1 = tr.G[3];
-            tr.n_streams = 2;
-        }
-    }
-    for (int si = 0; si < tr.n_streams; ++si)
-        tr.S[si].Wp = (int)ceil_div(tr.S[si].W, VW) * VW;
-    {
-        int co = 0;
-        MFM_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, device), "attribute");
-        // The persistent epoch loop (one cooperative launch per epoch) is opt-in:
-        // at 4096-row batches the per-batch launches are faster today.
-        const char* pe = getenv("MFM_B200_EPOCH_KERNEL");
-        tr.coop = co != 0 && pe && *pe == '1';
-        tr.bar.alloc(device, 1);
-    }
-    tr.grow.alloc(device, std::max<int64_t>(1, std::min(tr.B, n)) * C);
-
-    FwdArgs<T> A{};
-    A.indptr = tr.indptr.ptr;
-    A.indices = tr.indices.ptr;
-    A.data = tr.data.ptr;
-    A.y = tr.y.ptr;
-    A.ycls = tr.ycls.ptr;
-    A.sw = tr.sw.ptr;
-    A.C = C;
-    A.k = (int)k;
-    A.F = (int)F;
-    A.loss = c->loss;
-    A.multiclass = f.multiclass ? 1 : 0;
-    A.ls_on = (T)(1.0 - c->label_smoothing);
-    A.ls_off = (T)(C > 1 ? c->label_smoothing / ((double)C - 1.0) : 0.0);
-    A.w0 = tr.par[0].ptr;
-    A.w = tr.par[1].ptr;
-    A.v = tr.par[2].ptr;
-    A.r = tr.par[3].ptr;
-    A.fid = tr.fid.ptr;
-    A.grow = tr.grow.ptr;
+    FwdArgs<T> A = tr.prepare(f.tr, tr.data.ptr, tr.y.ptr, tr.ycls.ptr, tr.sw.ptr);
     pt.mark("upload");
     if (n > 0) tr.run(A, pt);
+    (void)F;
 
     tr.download_group(0, f.w0, 1, 1);
     tr.download_group(1, f.w, nf, 1);
@@ -1898,5 +1934,76 @@ extern "C" int mfm_fwfm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
         FitSpec f{M_FWFM, true, n_classes, x, nullptr, y, sample_weight, field_ids, n_fields,
                   tr, k, w0, w, v, r};
         fit_dispatch(f, ex);
+    });
+}
+
+// ---------------------------------------------------- device-resident fit --
+
+namespace mfm {
+template <class T>
+void fm_fit_device_impl(int device, cudaStream_t s, const int64_t* indptr,
+                        const int32_t* indices, const T* data, int64_t n_rows, int64_t n_features,
+                        const T* y, const T* sw, const int32_t* d_order, const mfm_train* c,
+                        int64_t k, const mfm_dev_group* w0, const mfm_dev_group* w,
+                        const mfm_dev_group* v) {
+    DeviceGuard guard(device);
+    std::lock_guard<std::mutex> lk(device_mutex(device));
+    Trainer<T> tr;
+    tr.device = device;
+    tr.s = s;
+    PhaseTimer pt(s);
+    tr.model = M_FM;
+    tr.C = 1;
+    tr.multiclass = false;
+    tr.n_rows = n_rows;
+    tr.n_feat = n_features;
+    tr.F = 1;
+    tr.k = k;
+    tr.B = c->batch_size;
+    tr.E = c->n_epochs;
+    tr.tr = c;
+    tr.nb = n_rows > 0 ? ceil_div(n_rows, tr.B) : 0;
+    tr.p_indptr = indptr;
+    tr.p_indices = indices;
+    tr.p_order = d_order;
+    tr.device_group(0, w0, 1, 1, 2);
+    tr.device_group(1, w, n_features, 1, 0);
+    tr.device_group(2, v, n_features * k, k, 1);
+    FwdArgs<T> A = tr.prepare(c, data, y, nullptr, sw);
+    pt.mark("setup");
+    if (n_rows > 0) tr.run(A, pt);
+}
+}  // namespace mfm
+
+extern "C" int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr,
+                                 const int32_t* indices, const void* data, int64_t n_rows,
+                                 int64_t n_features, const void* y, const void* sample_weight,
+                                 const int32_t* row_orders, const mfm_train* tr, int64_t k,
+                                 mfm_dev_group* w0, mfm_dev_group* w, mfm_dev_group* v,
+                                 void* stream) {
+    return guarded([&] {
+        if (!tr || tr->batch_size < 1) fail(MFM_ERR_INVALID, "batch_size must be >= 1");
+        if (tr->optimizer < MFM_OPT_SGD || tr->optimizer > MFM_OPT_FTRL)
+            fail(MFM_ERR_INVALID, fmt("unknown optimizer %d", tr->optimizer));
+        if (tr->loss != MFM_LOSS_LOGISTIC && tr->loss != MFM_LOSS_SQUARED)
+            fail(MFM_ERR_INVALID, fmt("unknown loss %d", tr->loss));
+        if (k < 1 || k > 1024)
+            fail(MFM_ERR_UNSUPPORTED,
+                 fmt("CUDA training supports 1 <= k <= 1024, got %lld", (long long)k));
+        if (n_rows < 0 || n_rows >= ((int64_t)1 << 31))
+            fail(MFM_ERR_UNSUPPORTED, "n_rows must be in [0, 2^31)");
+        if (!w0 || !w || !v || !w0->param || !w->param || !v->param)
+            fail(MFM_ERR_INVALID, "parameter arrays must be provided");
+        cudaStream_t s = (cudaStream_t)stream;
+        if (dtype == MFM_DTYPE_F32)
+            fm_fit_device_impl<float>(device, s, indptr, indices, (const float*)data, n_rows,
+                                      n_features, (const float*)y, (const float*)sample_weight,
+                                      row_orders, tr, k, w0, w, v);
+        else if (dtype == MFM_DTYPE_F64)
+            fm_fit_device_impl<double>(device, s, indptr, indices, (const double*)data, n_rows,
+                                       n_features, (const double*)y,
+                                       (const double*)sample_weight, row_orders, tr, k, w0, w, v);
+        else
+            fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
     });
 }

@@ -164,3 +164,54 @@ def test_f32_ftrl_fwfm_zero_pattern(monkeypatch):
         outs.append((wv, Vv, rv))
     np.testing.assert_array_equal(outs[0][0] == 0.0, outs[1][0] == 0.0)
     assert np.sum(outs[0][0] == 0.0) > 0
+
+
+@pytest.mark.parametrize("dtype,opt", [("float32", "adagrad"), ("float64", "adam"),
+                                       ("float32", "ftrl")])
+def test_device_resident_fit_matches_host_fit(dtype, opt):
+    """mfm_fm_fit_device on caller-owned device arrays gives exactly what the
+    host-buffer entry point gives (same kernels, same order)."""
+    import torch
+
+    from modern_fm_b200 import _lib
+
+    X, y, _ = workloads.onehot_ctr(3000, seed=6)
+    rng = np.random.default_rng(2)
+    d, k = X.n_features, 16
+    w_init, V_init = rng.normal(0, 0.01, d), rng.normal(0, 0.01, (d, k))
+    ro = workloads.row_orders(X.n_rows, 2, seed=8)
+    kw = dict(l1_linear=0.01, l1_factors=0.001) if opt == "ftrl" else {}
+    import os
+
+    os.environ["MFM_B200_DTYPE"] = dtype
+    try:
+        host = _fm_fit(_rust, X, y, np.ones(X.n_rows), (0.1, w_init, V_init), ro, 256, True,
+                       optimizer=opt, **kw)
+    finally:
+        del os.environ["MFM_B200_DTYPE"]
+    tdt = torch.float32 if dtype == "float32" else torch.float64
+    dev = torch.device("cuda", 0)
+    t = lambda a, dt=tdt: torch.as_tensor(np.ascontiguousarray(a), dtype=dt, device=dev)  # noqa
+    ip, ix, dv = t(X.indptr, torch.int64), t(X.indices, torch.int32), t(X.data)
+    yy, sw, rot = t(y), t(np.ones(X.n_rows)), t(ro, torch.int32)
+    w0, w, V = t([0.1]), t(w_init), t(V_init)
+    hp = dict(learning_rate=0.05, l2_linear=1e-5, l2_factors=1e-5)
+    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS[opt], hp["learning_rate"],
+                    kw.get("l1_linear", 0.0), hp["l2_linear"], kw.get("l1_factors", 0.0),
+                    hp["l2_factors"], 0.9, 0.999, 1e-8, 1.0, 0.0, None, ro.shape[0], 256)
+    g = [_lib.DevGroup(a.data_ptr(), None, None, None, None, None, None) for a in (w0, w, V)]
+    code = _lib.MFM_DTYPE_F32 if dtype == "float32" else _lib.MFM_DTYPE_F64
+    stream = torch.cuda.current_stream(dev)
+    rc = _lib.lib().mfm_fm_fit_device(code, 0, ip.data_ptr(), ix.data_ptr(), dv.data_ptr(),
+                                      X.n_rows, d, yy.data_ptr(), sw.data_ptr(), rot.data_ptr(),
+                                      tr, k, g[0], g[1], g[2], stream.cuda_stream)
+    assert rc == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert float(w0.item()) == float(np.float64(host[0]).astype(np.float32 if dtype == "float32"
+                                                             else np.float64))
+    np.testing.assert_array_equal(w.cpu().numpy().astype(np.float64),
+                                  host[1].astype(tdt == torch.float32 and np.float32
+                                                 or np.float64).astype(np.float64))
+    np.testing.assert_array_equal(V.cpu().numpy().astype(np.float64),
+                                  host[2].astype(tdt == torch.float32 and np.float32
+                                                 or np.float64).astype(np.float64))
