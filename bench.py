@@ -274,6 +274,20 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     if not np.isfinite(float(V.abs().max())):
         raise RuntimeError("training diverged")
 
+    out = {
+        "metric": "FM AdaGrad training rows/s (CTR-shaped 39 fields, 2^22 features, k=16, "
+                  "batch 4096, 1 epoch per step)",
+        "value": world * n / (ms / 1e3), "unit": "rows/s", "rows_per_gpu": n,
+        "steps": args.train_steps, "ms_per_step": ms, "scaling": "weak (independent fits)",
+    }
+    peak, _ = peaks()
+    achieved = bytes_epoch / (ms / 1e3) / 1e9
+    out["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                       "frac": achieved / peak, "bytes_per_epoch": bytes_epoch,
+                       "touched_per_epoch": touched}
+    if args.train_e2e_rows <= 0:
+        return out if rank == 0 else None
+
     # e2e: the reference-facing fit entry point with pinned host buffers in
     # the boundary format (int64 indices, float64 values / parameters / state)
     n_e = min(n, args.train_e2e_rows)
@@ -328,19 +342,8 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
                                          "(contiguous-chunk split, rust/src/fm.rs:286-311)"}
     if rank != 0:
         return None
-    peak, _ = peaks()
-    achieved = bytes_epoch / (ms / 1e3) / 1e9
-    out = {
-        "metric": "FM AdaGrad training rows/s (CTR-shaped 39 fields, 2^22 features, k=16, "
-                  "batch 4096, 1 epoch per step)",
-        "value": world * n / (ms / 1e3), "unit": "rows/s", "rows_per_gpu": n,
-        "steps": args.train_steps, "ms_per_step": ms, "scaling": "weak (independent fits)",
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "bytes_per_epoch": bytes_epoch,
-                     "touched_per_epoch": touched},
-        "e2e": {"value": world * n_e / e2e_s, "unit": "rows/s", "rows": n_e,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-    }
+    out["e2e"] = {"value": world * n_e / e2e_s, "unit": "rows/s", "rows": n_e,
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
     if cpu:
         out["cpu_baseline"] = cpu
     return out
@@ -358,6 +361,16 @@ def run_ours(args):
     dev_t = torch.device("cuda", local)
     torch.cuda.set_device(dev_t)
     L = _lib.lib()
+    if args.train_only:
+        train = train_measure(args, rank, world, local, dev_t, L, _lib)
+        if train:
+            train["n_gpus"] = world
+            print(json.dumps(train), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     X = WL.ctr_fm_torch(N_ROWS, SEED + rank, device=dev_t)
     w0, w64, V64 = make_params(local, dev_t)
     w32, V32 = w64.float().contiguous(), V64.float().contiguous()
@@ -531,6 +544,8 @@ def main():
     ap.add_argument("--rows", type=int, default=N_ROWS,
                     help="rows per GPU (smaller cases for profiling runs)")
     ap.add_argument("--no-train", action="store_true", help="skip the training measurement")
+    ap.add_argument("--train-only", action="store_true",
+                    help="only the training measurement (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS)
     ap.add_argument("--train-steps", type=int, default=2)

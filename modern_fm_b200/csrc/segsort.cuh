@@ -8,8 +8,12 @@
 //   3. seg_scatter_kernel: per tile, stable rank of each entry among equal
 //                          digits (warp match + per-warp counts) and scatter.
 // Stability makes the final order (key, original position) — deterministic,
-// with no floating point involved.
+// with no floating point involved. The last pass can replace each value by
+// data gathered through it (RecGather): the sorted stream then carries what
+// its consumer reads instead of an index into the unsorted one.
 #pragma once
+
+#include <type_traits>
 
 #include "scan.cuh"
 
@@ -53,12 +57,33 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// Value writers of the scatter: plain (the value itself) or, on the last
+// pass, two arrays gathered at segment start + value.
+struct PlainValue {
+    __device__ __forceinline__ void operator()(uint32_t* vout, int64_t dst, int64_t,
+                                               uint32_t val) const {
+        vout[dst] = val;
+    }
+};
+template <class T>
+struct RecGather {
+    const uint32_t* a;  // -> vout
+    const T* b;         // -> bout
+    T* bout;
+    __device__ __forceinline__ void operator()(uint32_t* vout, int64_t dst, int64_t seg0,
+                                               uint32_t val) const {
+        vout[dst] = a[seg0 + val];
+        bout[dst] = b[seg0 + val];
+    }
+};
+
+template <class Out>
 __global__ void __launch_bounds__(kSortNT)
     seg_scatter_kernel(const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin,
                        uint32_t* __restrict__ kout, uint32_t* __restrict__ vout,
                        const int64_t* __restrict__ tile_lo, const int64_t* __restrict__ tile_hi,
                        const int64_t* __restrict__ tile_seg_lo, int shift,
-                       const uint32_t* __restrict__ offs) {
+                       const uint32_t* __restrict__ offs, Out out) {
     __shared__ uint32_t wh[kSortNT / 32][256];  // per-warp digit counts -> prefixes
     __shared__ uint32_t running[256];
     __shared__ uint32_t round_tot[256];
@@ -97,7 +122,7 @@ __global__ void __launch_bounds__(kSortNT)
         if (valid) {
             const int64_t dst = seg0 + running[d] + wh[warp][d] + rank;
             kout[dst] = key;
-            vout[dst] = val;
+            out(vout, dst, seg0, val);
         }
         __syncthreads();
         if (t < 256) running[t] += round_tot[t];
@@ -131,16 +156,23 @@ __global__ void seg_tile_count_kernel(const int64_t* __restrict__ seg_lo, int64_
 // Sorts (keys, vals)[seg_lo[0], seg_lo[n_seg]) stably by key within each
 // segment; only the low `key_bits` bits are examined. Segments must be
 // shorter than 2^32 entries. Returns a pointer to whichever of the two
-// buffers holds the result.
+// buffers holds the result. With a RecGather `last`, the final pass writes
+// last.a[seg start + value] as the value and last.b[...] into last.bout
+// (at least one pass runs then, so the gather always happens). With kfirst
+// set, the first pass reads its keys there instead of k0 (kfirst is never
+// written; k0 only serves as scratch from the second pass on).
 struct SortResult {
     uint32_t* keys;
     uint32_t* vals;
 };
 
-inline SortResult segmented_sort(int device, cudaStream_t s, uint32_t* k0, uint32_t* v0,
-                                 uint32_t* k1, uint32_t* v1, const int64_t* d_seg_lo,
-                                 int64_t n_seg, int64_t n_entries, int key_bits) {
+template <class Last = PlainValue>
+SortResult segmented_sort(int device, cudaStream_t s, uint32_t* k0, uint32_t* v0, uint32_t* k1,
+                          uint32_t* v1, const int64_t* d_seg_lo, int64_t n_seg, int64_t n_entries,
+                          int key_bits, Last last = Last{}, const uint32_t* kfirst = nullptr) {
     SortResult res{k0, v0};
+    constexpr bool gather = !std::is_same<Last, PlainValue>::value;
+    if (gather && key_bits < 1) key_bits = 1;
     if (n_entries == 0 || key_bits <= 0 || n_seg == 0) return res;
     DevBuf<int64_t> seg_tile(device, n_seg + 1);
     seg_tile_count_kernel<<<(unsigned)ceil_div(n_seg, 256), 256, 0, s>>>(d_seg_lo, n_seg,
@@ -154,17 +186,27 @@ inline SortResult segmented_sort(int device, cudaStream_t s, uint32_t* k0, uint3
     seg_tiles_kernel<<<(unsigned)ceil_div(n_seg, 256), 256, 0, s>>>(
         d_seg_lo, n_seg, seg_tile.ptr, tlo.ptr, thi.ptr, tseg.ptr);
     DevBuf<uint32_t> hist(device, (size_t)n_tiles * 256);
-    uint32_t *ki = k0, *vi = v0, *ko = k1, *vo = v1;
+    const uint32_t* ki = kfirst ? kfirst : k0;
+    uint32_t *vi = v0, *ko = k1, *vo = v1;
     for (int shift = 0; shift < key_bits; shift += 8) {
         seg_hist_kernel<<<(unsigned)n_tiles, 256, 0, s>>>(ki, tlo.ptr, thi.ptr, shift, hist.ptr);
         seg_offsets_kernel<<<(unsigned)n_seg, 256, 0, s>>>(d_seg_lo, seg_tile.ptr, hist.ptr);
-        seg_scatter_kernel<<<(unsigned)n_tiles, kSortNT, 0, s>>>(ki, vi, ko, vo, tlo.ptr, thi.ptr,
-                                                                 tseg.ptr, shift, hist.ptr);
+        if (gather && shift + 8 >= key_bits)
+            seg_scatter_kernel<Last><<<(unsigned)n_tiles, kSortNT, 0, s>>>(
+                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, shift, hist.ptr, last);
+        else
+            seg_scatter_kernel<PlainValue><<<(unsigned)n_tiles, kSortNT, 0, s>>>(
+                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, shift, hist.ptr, PlainValue{});
         MFM_CHECK_LAUNCH("segmented sort launch");
-        std::swap(ki, ko);
-        std::swap(vi, vo);
+        // the next pass reads what this one wrote and writes the other pair
+        uint32_t* nk = ko == k1 ? k0 : k1;
+        uint32_t* nv = vo == v1 ? v0 : v1;
+        ki = ko;
+        vi = vo;
+        ko = nk;
+        vo = nv;
     }
-    res.keys = ki;
+    res.keys = const_cast<uint32_t*>(ki);
     res.vals = vi;
     return res;
 }

@@ -31,6 +31,7 @@
 //       fixed order and applies; its last block steps w0 from the per-row
 //       gradients.
 #include <algorithm>
+#include <utility>
 #include <cmath>
 
 #include "segsort.cuh"
@@ -55,6 +56,18 @@ struct OptDev {
     double lr, b1, b2, eps, fbeta;
     double l1[3], l2[3];
 };
+
+// Programmatic dependent launch (sm_90+): a kernel launched with the
+// programmatic-serialization attribute may start while its predecessor in the
+// stream drains. pdl_trigger lets the successor be scheduled once every block
+// of this grid has started; pdl_wait blocks until the predecessor grid has
+// completed and its writes are visible (immediately when launched normally).
+// Every thread of a PDL kernel calls pdl_wait before its first write and
+// before it exits, so this grid's completion implies its predecessor's.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // One step of the reference's step_param / step_coord (rust/src/optimizer.rs:
 // 48-167) for coordinate idx of group g with batch-mean data gradient dg.
@@ -109,12 +122,29 @@ __device__ __forceinline__ void opt_step(const GroupDev<T>& g, int64_t idx, T dg
 // opt_step on VEC consecutive coordinates [idx0, idx0 + VEC) of one group,
 // with 16-byte loads and stores of the parameter and its state. The state is
 // loaded before the gradients are known (`prefetch`) so the loads overlap the
-// payload reduction; `commit` applies the step.
-template <class T, int VEC>
+// payload reduction; `commit` applies the step. OPT >= 0 fixes the optimizer
+// at compile time (only its state vectors occupy registers).
+template <class T, int VEC, int OPT = -1>
 struct VecStep {
     Vec<T, VEC> p, a, b, c;  // param and up to three state vectors
-    __device__ __forceinline__ void prefetch(const GroupDev<T>& g, int64_t idx0, int kind) {
+    __device__ __forceinline__ void prefetch(const GroupDev<T>& g, int64_t idx0, int kind_rt) {
+        const int kind = OPT >= 0 ? OPT : kind_rt;
         p = ldg_vec<T, VEC>(g.p + idx0);
+        if (kind == MFM_OPT_ADAGRAD) {
+            a = ldg_vec<T, VEC>(g.acc + idx0);
+        } else if (kind == MFM_OPT_ADAM) {
+            a = ldg_vec<T, VEC>(g.m + idx0);
+            b = ldg_vec<T, VEC>(g.s + idx0);
+            c = ldg_vec<T, VEC>(g.t + idx0);
+        } else if (kind == MFM_OPT_FTRL) {
+            a = ldg_vec<T, VEC>(g.z + idx0);
+            b = ldg_vec<T, VEC>(g.n + idx0);
+        }
+    }
+    // the state only (the caller already holds the parameter vector in p)
+    __device__ __forceinline__ void prefetch_state(const GroupDev<T>& g, int64_t idx0,
+                                                   int kind_rt) {
+        const int kind = OPT >= 0 ? OPT : kind_rt;
         if (kind == MFM_OPT_ADAGRAD) {
             a = ldg_vec<T, VEC>(g.acc + idx0);
         } else if (kind == MFM_OPT_ADAM) {
@@ -129,10 +159,11 @@ struct VecStep {
     __device__ __forceinline__ void commit(const GroupDev<T>& g, int64_t idx0, const T* dg,
                                            const OptDev& o) {
         const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
+        const int kind = OPT >= 0 ? OPT : o.kind;
 #pragma unroll
         for (int u = 0; u < VEC; ++u) {
             T th = p.v[u];
-            switch (o.kind) {
+            switch (kind) {
             case MFM_OPT_SGD:
                 th -= lr * (dg[u] + l2 * th);
                 break;
@@ -175,13 +206,13 @@ struct VecStep {
             p.v[u] = th;
         }
         *reinterpret_cast<Vec<T, VEC>*>(g.p + idx0) = p;
-        if (o.kind == MFM_OPT_ADAGRAD) {
+        if (kind == MFM_OPT_ADAGRAD) {
             *reinterpret_cast<Vec<T, VEC>*>(g.acc + idx0) = a;
-        } else if (o.kind == MFM_OPT_ADAM) {
+        } else if (kind == MFM_OPT_ADAM) {
             *reinterpret_cast<Vec<T, VEC>*>(g.m + idx0) = a;
             *reinterpret_cast<Vec<T, VEC>*>(g.s + idx0) = b;
             *reinterpret_cast<Vec<T, VEC>*>(g.t + idx0) = c;
-        } else if (o.kind == MFM_OPT_FTRL) {
+        } else if (kind == MFM_OPT_FTRL) {
             *reinterpret_cast<Vec<T, VEC>*>(g.z + idx0) = a;
             *reinterpret_cast<Vec<T, VEC>*>(g.n + idx0) = b;
         }
@@ -232,6 +263,19 @@ __global__ void count_kernel(int kind, const int32_t* __restrict__ order,
     cnt[i] = stream_count(kind, indptr[row + 1] - indptr[row]);
 }
 
+// y and sample weight in epoch order (row-table path: the forward reads rows
+// by epoch position).
+template <class T>
+__global__ void permute_rows_kernel(const int32_t* __restrict__ order, const T* __restrict__ y,
+                                    const T* __restrict__ sw, int64_t n_rows, T* __restrict__ py,
+                                    T* __restrict__ psw) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_rows) return;
+    const int64_t row = order[i];
+    py[i] = y[row];
+    psw[i] = sw[row];
+}
+
 __global__ void seg_lo_kernel(const int64_t* __restrict__ estart, int64_t n_rows, int64_t B,
                               int64_t nb, int64_t* __restrict__ seg_lo) {
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -249,12 +293,17 @@ __device__ __forceinline__ void pair_step(int64_t& a, int64_t& b, int64_t z) {
 
 // One warp per epoch position: writes the keys and batch-local entry ids of
 // the row's entries, in the order the forward kernel writes their payloads.
+// With erow set (FEAT only), also each entry's batch-local row and value, for
+// the row-table reduction.
+template <class T>
 __global__ void __launch_bounds__(256)
     expand_kernel(int kind, const int32_t* __restrict__ order, const int64_t* __restrict__ indptr,
                   const int32_t* __restrict__ indices, const int32_t* __restrict__ fid, int F,
                   int64_t n_rows, int64_t B, const int64_t* __restrict__ estart,
                   const int64_t* __restrict__ seg_lo, uint32_t* __restrict__ keys,
-                  uint32_t* __restrict__ vals) {
+                  uint32_t* __restrict__ vals, const T* __restrict__ data,
+                  uint32_t* __restrict__ erow, T* __restrict__ ex) {
+    // (FEAT with erow: keys[] is kept unsorted as the epoch-order CSR indices)
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t pos = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; pos < n_rows;
@@ -265,9 +314,14 @@ __global__ void __launch_bounds__(256)
         const int64_t base = estart[pos];
         const int64_t local = base - seg_lo[pos / B];
         if (kind == FEAT) {
+            const uint32_t rib = (uint32_t)(pos % B);
             for (int64_t a = lane; a < z; a += 32) {
                 keys[base + a] = (uint32_t)ix[a];
                 vals[base + a] = (uint32_t)(local + a);
+                if (erow) {
+                    erow[base + a] = rib;
+                    ex[base + a] = data[rb + a];
+                }
             }
         } else if (kind == SLOT) {  // ordered pairs (a, b != a): key = i_a * F + f_b
             const int64_t tot = z * (z - 1);
@@ -399,6 +453,8 @@ struct FwdArgs {
     T* pay2;
     int W2;
     T* grow;  // (nrows, C) per-row loss gradients, summed into the w0 gradient
+    T* tab;   // row table (nrows, TW): [S (k) | g | pad] (binary FM row-table path)
+    int TW;
 };
 
 template <class T>
@@ -557,7 +613,8 @@ __device__ __forceinline__ void rows_gather(const FwdArgs<T>& A, int64_t rb, int
                                             int64_t base, int rl, int grp, int l, bool act,
                                             int (&nh)[RowsShape<T, VEC, L, LR, CAP>::NC],
                                             Vec<T, VEC> (&q)[RowsShape<T, VEC, L, LR, CAP>::S],
-                                            T (&xs)[RowsShape<T, VEC, L, LR, CAP>::S], T& lin) {
+                                            T (&xs)[RowsShape<T, VEC, L, LR, CAP>::S], T& lin,
+                                            bool pdl = false) {
     using Sh = RowsShape<T, VEC, L, LR, CAP>;
     int32_t ii[Sh::NC];
     T xx[Sh::NC];
@@ -572,6 +629,7 @@ __device__ __forceinline__ void rows_gather(const FwdArgs<T>& A, int64_t rb, int
             xx[c] = A.data[rb + base + LR * c + rl];
         }
     }
+    if (pdl) pdl_wait();  // parameters below are the predecessor's output
 #pragma unroll
     for (int c = 0; c < Sh::NC; ++c)
         if (rl < nh[c]) lin += A.w[ii[c]] * xx[c];
@@ -615,17 +673,20 @@ __device__ __forceinline__ void rows_payload(const FwdArgs<T>& A, int64_t e0, in
     }
 }
 
-template <class T, int VEC, int L, int LR, int CAP>
+// TAB: write the row table [S | g] instead of per-entry payloads.
+template <class T, int VEC, int L, int LR, int CAP, bool TAB = false>
 __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t slot0,
                                                     int64_t nslots) {
     using Sh = RowsShape<T, VEC, L, LR, CAP>;
     const int lane = threadIdx.x & 31, rl = lane & (LR - 1), grp = rl / L, l = rl % L;
     const bool act = l < A.k / VEC;
+    if (TAB) pdl_trigger();
     for (int64_t j = slot0;; j += nslots) {
         const bool live = j < A.nrows;
         if (!__any_sync(0xffffffffu, live)) break;
         const int64_t pos = A.pos0 + j;
-        const int64_t row = live ? A.order[pos] : 0;
+        // TAB: CSR, y and sample weight are already in epoch order
+        const int64_t row = live ? (TAB ? pos : A.order[pos]) : 0;
         const int64_t rb = live ? A.indptr[row] : 0;
         const int64_t z = live ? A.indptr[row + 1] - rb : 0;
         // pass 1: score from the frozen parameters (train_score_row, fm.rs:77-101)
@@ -639,7 +700,7 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
         int iters = 0;
         for (int64_t base = 0;; base += CAP, ++iters) {
             if (!__any_sync(0xffffffffu, base < z)) break;
-            rows_gather<T, VEC, L, LR, CAP>(A, rb, z, base, rl, grp, l, act, nh, q, xs, lin);
+            rows_gather<T, VEC, L, LR, CAP>(A, rb, z, base, rl, grp, l, act, nh, q, xs, lin, TAB);
 #pragma unroll
             for (int st = 0; st < Sh::S; ++st)
 #pragma unroll
@@ -662,10 +723,24 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
 #pragma unroll
         for (int o = LR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
         T g = T(0);
+        if (TAB) pdl_wait();  // w0 and the writes below follow the predecessor
         if (live) {  // loss_grad x sample_weight, optimizer.rs:38-43
             const T s = A.w0[0] + t, y = A.y[row];
             g = A.sw[row] * (A.loss == MFM_LOSS_LOGISTIC ? sigmoid_t(s) - y : s - y);
             if (rl == 0) A.grow[j] = g;
+        }
+        if (TAB) {
+            if (live) {
+                T* tr = A.tab + j * A.TW;
+                if (grp == 0 && act) {
+                    Vec<T, VEC> o;
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) o.v[u] = cache[u];
+                    *reinterpret_cast<Vec<T, VEC>*>(tr + l * VEC) = o;
+                }
+                if (rl == 0) tr[A.k] = g;
+            }
+            continue;
         }
         // pass 2: payload rows at their sorted positions
         const int64_t e0 = live ? A.estart1[pos] - A.seg1 : 0;
@@ -680,11 +755,12 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
             }
         }
     }
+    if (TAB) pdl_wait();
 }
 
-template <class T, int VEC, int L, int LR, int CAP>
+template <class T, int VEC, int L, int LR, int CAP, bool TAB = false>
 __global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
-    fm_forward_rows_dev<T, VEC, L, LR, CAP>(
+    fm_forward_rows_dev<T, VEC, L, LR, CAP, TAB>(
         A, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR,
         ((int64_t)gridDim.x * blockDim.x) / LR);
 }
@@ -946,19 +1022,34 @@ __global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t
 // w0: the batch's per-row gradients summed in a fixed tree by one block,
 // then one step per class (step_param with l1 = l2 = 0, optimizer.rs:114-135).
 template <class T>
-__device__ __forceinline__ void w0_dev(const RedArgs<T>& R, T* sm) {
-    for (int c = 0; c < R.C; ++c) {
+__device__ __forceinline__ void w0_step_dev(const T* grow, int64_t nrows, int C, T inv_bsz,
+                                            const GroupDev<T>& gw0, const OptDev& opt, T* sm) {
+    for (int c = 0; c < C; ++c) {
         T s = T(0);
-        for (int64_t j = threadIdx.x; j < R.nrows; j += blockDim.x) s += R.grow[j * R.C + c];
+        const int64_t bd = blockDim.x;
+        int64_t j = threadIdx.x;
+        for (; j + 7 * bd < nrows; j += 8 * bd) {  // eight loads in flight, same order
+            T a[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) a[u] = grow[(j + u * bd) * C + c];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) s += a[u];
+        }
+        for (; j < nrows; j += bd) s += grow[j * C + c];
         sm[threadIdx.x] = s;
         __syncthreads();
         for (int h = blockDim.x / 2; h > 0; h >>= 1) {
             if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
             __syncthreads();
         }
-        if (threadIdx.x == 0) opt_step(R.gw0, c, sm[0] * R.inv_bsz, R.opt);
+        if (threadIdx.x == 0) opt_step(gw0, c, sm[0] * inv_bsz, opt);
         __syncthreads();
     }
+}
+
+template <class T>
+__device__ __forceinline__ void w0_dev(const RedArgs<T>& R, T* sm) {
+    w0_step_dev(R.grow, R.nrows, R.C, R.inv_bsz, R.gw0, R.opt, sm);
 }
 
 template <class T, int VEC>
@@ -1033,6 +1124,261 @@ __global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t 
         return;
     }
     reduce_runs_dev<T, VEC>(R, l0, n_long, blockIdx.x, gridDim.x - 1, wsum);
+}
+
+// ------------------------------------------ binary FM row-table reduction --
+//
+// Binary FM with k = NV * VEC (16-byte vectors, NV <= 8). The forward writes
+// one table row per batch row, [S (k) | g | pad], S = sum_j V_j x_j the row's
+// factor sum and g = dL/ds x sample weight. The reduction reads the batch's
+// sorted entry stream (key, row, x) and recomputes each entry's gradient from
+// the table exactly as FmGradAccum::add_row forms it (rust/src/fm.rs:136-146):
+//   gv[t] = g (x S[t] - V[t] x x),   gw = g x,
+// so no per-entry payload is ever written.
+//
+// Stage 1: one block per chunk of kChunk consecutive sorted entries, one
+// entry per thread; a segmented shuffle reduction per warp, then the warps'
+// pieces of a segment folded in warp order; the owner of a segment (its first
+// entry) applies the optimizer. A segment continued from the previous chunk
+// leaves its sum in ph[chunk]; the last segment, when it continues into the
+// next chunk, leaves its sum in pt[chunk].
+// Stage 2: one warp per chunk boundary that starts a crossing run folds
+// pt[first chunk] + ph[...] in chunk order and applies; the last block steps
+// w0. Every sum has a fixed shape, so results are bitwise reproducible.
+
+constexpr int kChunk = 256;
+
+template <class T>
+struct TabArgs {
+    const uint32_t* keys;  // sorted keys of the epoch's entry stream
+    const uint32_t* rrow;  // batch-local row of each sorted entry
+    const T* rx;           // value of each sorted entry
+    const T* tab;          // (nrows, TW) [S | g | pad]
+    T* ph;                 // (chunks, TW) sums continued from the previous chunk
+    T* pt;                 // (chunks, TW) sums continued into the next chunk
+    int TW;
+    int64_t seg, n;        // this batch's entries: [seg, seg + n) of the sorted stream
+    int64_t nrows;
+    const T* grow;         // per-row g, for w0
+    T inv_bsz;
+    GroupDev<T> gv, gw, gw0;
+    OptDev opt;
+};
+
+// float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
+template <class T, int NV, int OPT>
+constexpr int tab_min_blocks() {
+    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 4 : 1;
+}
+
+template <class T, int VEC, int NV, int OPT>
+__global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab_reduce_kernel(TabArgs<T> A) {
+    constexpr int K = VEC * NV, NVAL = K + 1, NW = kChunk / 32;
+    __shared__ __align__(16) T wpart[NW][NVAL];
+    __shared__ int wflag[NW];  // bit 0: lane 0 continues the previous warp; bit 1: one segment
+    __shared__ uint32_t s_last;
+    __shared__ int s_out;
+    const unsigned FULL = 0xffffffffu;
+    pdl_trigger();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t c0 = (int64_t)blockIdx.x * kChunk, i = c0 + tid;
+    const int64_t cend = c0 + kChunk < A.n ? c0 + kChunk : A.n;
+    const bool valid = i < A.n;
+    const int64_t gi = A.seg + i;
+    // prologue on the plan's arrays (not written by the predecessor)
+    if (tid == 0) {
+        const uint32_t lk = A.keys[A.seg + cend - 1];
+        s_last = lk;
+        s_out = cend < A.n && A.keys[A.seg + cend] == lk;
+    }
+    uint32_t key = 0, row = 0;
+    T x = T(0);
+    if (valid) {
+        key = A.keys[gi];
+        row = A.rrow[gi];
+        x = A.rx[gi];
+    }
+    uint32_t kprev = __shfl_up_sync(FULL, key, 1);
+    if (lane == 0) kprev = (valid && i > 0) ? A.keys[gi - 1] : ~key;
+    const bool rhead = valid && (i == 0 || key != kprev);
+    // warp segments start at real heads, at lane 0 and at every invalid lane
+    const unsigned hm = __ballot_sync(FULL, rhead || lane == 0 || !valid);
+    const unsigned after = hm & ~((2u << lane) - 1u);
+    const int send = after ? __ffs(after) - 2 : 31;
+
+    pdl_wait();  // the row table and the parameters are the predecessors' output
+    T val[NVAL];
+    if (valid) {
+        const T* tr = A.tab + (int64_t)row * A.TW;
+        const T* vp = A.gv.p + (int64_t)key * K;
+        const T g = tr[K];
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            const Vec<T, VEC> sv = ldg_vec<T, VEC>(tr + v * VEC);
+            const Vec<T, VEC> vk = ldg_vec<T, VEC>(vp + v * VEC);
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) val[v * VEC + u] = g * (x * sv.v[u] - vk.v[u] * x * x);
+        }
+        val[K] = g * x;
+    } else {
+#pragma unroll
+        for (int q = 0; q < NVAL; ++q) val[q] = T(0);
+    }
+    // segmented suffix sums: lane l ends with the sum over [l, send]
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const bool take = lane + o <= send;
+#pragma unroll
+        for (int q = 0; q < NVAL; ++q) {
+            const T y = __shfl_down_sync(FULL, val[q], o);
+            if (take) val[q] += y;
+        }
+    }
+    if (lane == 0) {
+        const bool cont = valid && !rhead && warp > 0;
+        wflag[warp] = (cont ? 1 : 0) | (send == 31 ? 2 : 0);
+        if (cont)
+#pragma unroll
+            for (int q = 0; q < NVAL; ++q) wpart[warp][q] = val[q];
+    }
+    __syncthreads();
+    const bool owner = valid && (rhead || tid == 0);
+    if (!owner) return;
+    if (send == 31)
+        for (int w2 = warp + 1; w2 < NW; ++w2) {
+            const int f = wflag[w2];
+            if (!(f & 1)) break;
+#pragma unroll
+            for (int q = 0; q < NVAL; ++q) val[q] += wpart[w2][q];
+            if (!(f & 2)) break;
+        }
+    const int64_t cb = blockIdx.x;
+    T* dst = nullptr;
+    if (tid == 0 && !rhead)
+        dst = A.ph + cb * A.TW;
+    else if (s_out && key == s_last)
+        dst = A.pt + cb * A.TW;
+    if (dst) {
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            Vec<T, VEC> o;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) o.v[u] = val[v * VEC + u];
+            *reinterpret_cast<Vec<T, VEC>*>(dst + v * VEC) = o;
+        }
+        dst[K] = val[K];
+        return;
+    }
+    // the whole run lies in this chunk: one optimizer step per coordinate
+    VecStep<T, VEC, OPT> st[NV];
+    VecStep<T, 1, OPT> sw1;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) st[v].prefetch(A.gv, (int64_t)key * K + v * VEC, A.opt.kind);
+    sw1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+        T dg[VEC];
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) dg[u] = val[v * VEC + u] * A.inv_bsz;
+        st[v].commit(A.gv, (int64_t)key * K + v * VEC, dg, A.opt);
+    }
+    const T dgw = val[K] * A.inv_bsz;
+    sw1.commit(A.gw, (int64_t)key, &dgw, A.opt);
+}
+
+template <class T, int VEC, int NV>
+__global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t nchunks) {
+    constexpr int K = VEC * NV;
+    const unsigned FULL = 0xffffffffu;
+    pdl_trigger();
+    if (blockIdx.x == gridDim.x - 1) {
+        __shared__ T sm[256];
+        pdl_wait();
+        w0_step_dev(A.grow, A.nrows, 1, A.inv_bsz, A.gw0, A.opt, sm);
+        return;
+    }
+    const int lane = threadIdx.x & 31;
+    const int64_t c = (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) + 1;
+    if (c >= nchunks) {  // uniform per warp
+        pdl_wait();
+        return;
+    }
+    // prologue on the sorted keys: lane i reads the first key of chunk c + i;
+    // lane 0 also the keys just before chunks c and c - 1
+    const int64_t jl = c + lane;
+    const uint32_t fk = jl < nchunks ? A.keys[A.seg + jl * kChunk] : 0u;
+    uint32_t kb = 0, kq = 0;
+    if (lane == 0) {
+        kb = A.keys[A.seg + c * kChunk - 1];
+        kq = c >= 2 ? A.keys[A.seg + (c - 1) * kChunk - 1] : 0u;
+    }
+    const uint32_t key = __shfl_sync(FULL, fk, 0);
+    const int stop = lane == 0 ? (kb != key || (c >= 2 && kq == key)) : 0;
+    // boundary c is not crossed, or is not the run's first crossed boundary
+    if (__shfl_sync(FULL, stop, 0)) {
+        pdl_wait();
+        return;
+    }
+    int ones = __popc(__ballot_sync(FULL, jl < nchunks && fk == key));
+    int64_t j1 = c + ones - 1;  // last chunk whose ph belongs to the run (keys are sorted)
+    for (int64_t jb = c + 32; ones == 32; jb += 32) {
+        const int64_t j = jb + lane;
+        ones = __popc(__ballot_sync(FULL, j < nchunks && A.keys[A.seg + j * kChunk] == key));
+        j1 = jb + ones - 1;
+    }
+    pdl_wait();  // the partials and the parameters are the predecessors' output
+    // the run's partials: element 0 = pt[c - 1], element e >= 1 = ph[c + e - 1];
+    // each lane loads one element, a butterfly folds every 32 of them (all
+    // lanes end with the same bits), the groups of 32 are added in order
+    const int64_t cnt = j1 - c + 2;
+    const int own = lane < NV ? lane : NV;  // column vector this lane applies (NV = w)
+    VecStep<T, VEC> st;
+    VecStep<T, 1> s1;
+    if (lane < NV)
+        st.prefetch(A.gv, (int64_t)key * K + lane * VEC, A.opt.kind);
+    else if (lane == NV)
+        s1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+    T tot[K + 1];
+#pragma unroll
+    for (int q = 0; q <= K; ++q) tot[q] = T(0);
+    for (int64_t e0 = 0; e0 < cnt; e0 += 32) {
+        const int64_t e = e0 + lane;
+        T part[K + 1];
+        if (e < cnt) {
+            const T* r = e == 0 ? A.pt + (c - 1) * A.TW : A.ph + (c + e - 1) * A.TW;
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                const Vec<T, VEC> x = ldg_vec<T, VEC>(r + v * VEC);
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) part[v * VEC + u] = x.v[u];
+            }
+            part[K] = r[K];
+        } else {
+#pragma unroll
+            for (int q = 0; q <= K; ++q) part[q] = T(0);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int q = 0; q <= K; ++q) part[q] += __shfl_xor_sync(FULL, part[q], o);
+#pragma unroll
+        for (int q = 0; q <= K; ++q) tot[q] += part[q];
+    }
+    if (lane < NV) {
+        T dg[VEC];
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) {
+            T t = T(0);
+#pragma unroll
+            for (int v = 0; v < NV; ++v)
+                if (v == own) t = tot[v * VEC + u];
+            dg[u] = t * A.inv_bsz;
+        }
+        st.commit(A.gv, (int64_t)key * K + lane * VEC, dg, A.opt);
+    } else if (lane == NV) {
+        const T dg = tot[K] * A.inv_bsz;
+        s1.commit(A.gw, (int64_t)key, &dg, A.opt);
+    }
 }
 
 // --------------------------------------------------- persistent epoch loop --
@@ -1168,6 +1514,33 @@ struct PhaseTimer {
     }
 };
 
+// Launch with programmatic stream serialization (see pdl_wait): the kernel may
+// start while its predecessor in the stream drains. MFM_B200_PDL=0 turns the
+// attribute off (plain stream order; the kernels' waits return at once).
+inline bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("MFM_B200_PDL");
+        return !(e && *e == '0');
+    }();
+    return on;
+}
+
+template <class... KArgs, class... Args>
+void launch_pdl(void (*kern)(KArgs...), unsigned grid, unsigned block, cudaStream_t s,
+                Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    MFM_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), "kernel launch");
+}
+
 unsigned blocks_for(int64_t n, int nt) { return (unsigned)std::max<int64_t>(1, ceil_div(n, nt)); }
 
 int bits_for(int64_t n_keys) {
@@ -1191,6 +1564,13 @@ struct Stream {
     std::vector<int64_t> h_seg, h_item, h_long;
     int64_t max_entries = 0, max_items = 0;
     DevBuf<T> pay, part;
+    // binary FM row-table path: sorted (key, row, x) entries, the row table
+    // and the chunk partials
+    bool tab = false;
+    int TW = 0;
+    DevBuf<uint32_t> erow, pidx;  // pidx: keys in epoch entry order (CSR indices by position)
+    DevBuf<T> ex, rx, table, ph, pt, py, psw;
+    uint32_t* rrow = nullptr;
 };
 
 template <class T>
@@ -1212,6 +1592,9 @@ struct Trainer {
     const int32_t* p_indices = nullptr;
     const int32_t* p_order = nullptr;
     const int32_t* p_fid = nullptr;
+    const T* p_data = nullptr;
+    const T* p_y = nullptr;
+    const T* p_sw = nullptr;
     // parameters + state per group: 0 = w0, 1 = w, 2 = V, 3 = R
     DevBuf<T> par[4], st[4][6];
     GroupDev<T> G[4] = {};
@@ -1310,10 +1693,41 @@ struct Trainer {
             st_.k1.alloc(device, N);
             st_.v1.alloc(device, N);
         }
-        expand_kernel<<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
+        if (st_.tab && (st_.erow.n < (size_t)N || !st_.erow.ptr)) {
+            st_.erow.alloc(device, std::max<int64_t>(N, 1));
+            st_.pidx.alloc(device, std::max<int64_t>(N, 1));
+            st_.ex.alloc(device, std::max<int64_t>(N, 1));
+            st_.rx.alloc(device, std::max<int64_t>(N, 1));
+        }
+        expand_kernel<T><<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
             st_.kind, order, p_indptr, p_indices, p_fid, (int)F, n_rows, B,
-            st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr);
+            st_.estart.ptr, st_.seg_lo.ptr, st_.tab ? st_.pidx.ptr : st_.k0.ptr, st_.v0.ptr,
+            p_data, st_.tab ? st_.erow.ptr : nullptr, st_.tab ? st_.ex.ptr : nullptr);
         MFM_CHECK_LAUNCH("expand");
+        if (st_.tab) {
+            // epoch-order CSR (estart, pidx, ex) + labels for the forward; sorted
+            // (key, row, x) for the reduction; chunk partials for the largest batch
+            if (st_.py.n < (size_t)n_rows || !st_.py.ptr) {
+                st_.py.alloc(device, n_rows);
+                st_.psw.alloc(device, n_rows);
+            }
+            permute_rows_kernel<T><<<blocks_for(n_rows, 256), 256, 0, s>>>(
+                order, p_y, p_sw, n_rows, st_.py.ptr, st_.psw.ptr);
+            SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr,
+                                           st_.v1.ptr, st_.seg_lo.ptr, nb, N,
+                                           bits_for(st_.n_keys),
+                                           RecGather<T>{st_.erow.ptr, st_.ex.ptr, st_.rx.ptr},
+                                           st_.pidx.ptr);
+            st_.keys = sr.keys;
+            st_.rrow = sr.vals;
+            const int64_t mc = std::max<int64_t>(1, ceil_div(st_.max_entries, kChunk));
+            if (st_.ph.n < (size_t)(mc * st_.TW) || !st_.ph.ptr) {
+                st_.ph.alloc(device, mc * st_.TW);
+                st_.pt.alloc(device, mc * st_.TW);
+            }
+            MFM_CHECK_LAUNCH("plan");
+            return;
+        }
         SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr,
                                        st_.seg_lo.ptr, nb, N, bits_for(st_.n_keys));
         st_.keys = sr.keys;
@@ -1442,6 +1856,14 @@ struct Trainer {
             }
         }
         for (int si = 0; si < n_streams; ++si) S[si].Wp = (int)ceil_div(S[si].W, VW) * VW;
+        // binary FM with k = NV * VW, NV in {1, 2, 4, 8}: row-table reduction
+        const int64_t nvw = k / VW;
+        if (model == M_FM && !multiclass && k % VW == 0 &&
+            (nvw == 1 || nvw == 2 || nvw == 4 || nvw == 8)) {
+            s0.tab = true;
+            s0.TW = (int)k + VW;
+            s0.table.alloc(device, std::max<int64_t>(1, std::min(B, n_rows)) * s0.TW);
+        }
         int co = 0;
         MFM_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, device), "attribute");
         // The persistent epoch loop (one cooperative launch per epoch) is opt-in:
@@ -1470,6 +1892,11 @@ struct Trainer {
         A.r = G[3].p;
         A.fid = p_fid;
         A.grow = grow.ptr;
+        A.tab = s0.table.ptr;
+        A.TW = s0.TW;
+        p_data = data;
+        p_y = yv;
+        p_sw = swv;
         return A;
     }
 
@@ -1508,8 +1935,11 @@ struct Trainer {
 #define MFM_FROWS(L_, LR_, CAP_)                                                            \
     {                                                                                       \
         const int64_t want = ceil_div(nrows * LR_, 256);                                    \
-        fm_forward_rows_kernel<T, VW, L_, LR_, CAP_>                                        \
-            <<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(g, want)), 256, 0, s>>>(A); \
+        const unsigned gr = (unsigned)std::max<int64_t>(1, std::min<int64_t>(g, want));     \
+        if (S[0].tab)                                                                       \
+            launch_pdl(fm_forward_rows_kernel<T, VW, L_, LR_, CAP_, true>, gr, 256, s, A);  \
+        else                                                                                \
+            fm_forward_rows_kernel<T, VW, L_, LR_, CAP_><<<gr, 256, 0, s>>>(A);             \
         MFM_CHECK_LAUNCH("FM forward");                                                     \
         return;                                                                             \
     }
@@ -1570,6 +2000,61 @@ struct Trainer {
         MFM_CHECK_LAUNCH("forward");
     }
 
+    // Row-table reduction of batch b (binary FM): stage 1 per chunk, stage 2
+    // per crossing run + w0.
+    template <int NV>
+    void launch_tab_t(const TabArgs<T>& TA, int64_t nchunks) {
+        constexpr int VW = 16 / (int)sizeof(T);
+        if (nchunks > 0) {
+            const unsigned g = (unsigned)nchunks;
+            switch (TA.opt.kind) {
+            case MFM_OPT_SGD:
+                launch_pdl(fm_tab_reduce_kernel<T, VW, NV, MFM_OPT_SGD>, g, kChunk, s, TA);
+                break;
+            case MFM_OPT_ADAGRAD:
+                launch_pdl(fm_tab_reduce_kernel<T, VW, NV, MFM_OPT_ADAGRAD>, g, kChunk, s, TA);
+                break;
+            case MFM_OPT_ADAM:
+                launch_pdl(fm_tab_reduce_kernel<T, VW, NV, MFM_OPT_ADAM>, g, kChunk, s, TA);
+                break;
+            default:
+                launch_pdl(fm_tab_reduce_kernel<T, VW, NV, MFM_OPT_FTRL>, g, kChunk, s, TA);
+            }
+        }
+        const int64_t warps = std::max<int64_t>(0, nchunks - 1);
+        launch_pdl(fm_tab_fold_kernel<T, VW, NV>, (unsigned)(ceil_div(warps, 8) + 1), 256, s, TA,
+                   nchunks);
+        MFM_CHECK_LAUNCH("row-table reduction");
+    }
+    void launch_tab(int64_t b, T inv_bsz, int64_t nrows) {
+        constexpr int VW = 16 / (int)sizeof(T);
+        Stream<T>& st_ = S[0];
+        TabArgs<T> TA;
+        TA.keys = st_.keys;
+        TA.rrow = st_.rrow;
+        TA.rx = st_.rx.ptr;
+        TA.tab = st_.table.ptr;
+        TA.ph = st_.ph.ptr;
+        TA.pt = st_.pt.ptr;
+        TA.TW = st_.TW;
+        TA.seg = st_.h_seg[b];
+        TA.n = st_.h_seg[b + 1] - st_.h_seg[b];
+        TA.nrows = nrows;
+        TA.grow = grow.ptr;
+        TA.inv_bsz = inv_bsz;
+        TA.gv = G[2];
+        TA.gw = G[1];
+        TA.gw0 = G[0];
+        TA.opt = opt;
+        const int64_t nchunks = ceil_div(TA.n, kChunk);
+        switch (k / VW) {
+        case 1: launch_tab_t<1>(TA, nchunks); break;
+        case 2: launch_tab_t<2>(TA, nchunks); break;
+        case 4: launch_tab_t<4>(TA, nchunks); break;
+        default: launch_tab_t<8>(TA, nchunks); break;
+        }
+    }
+
     void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz, int64_t nrows, bool do_w0) {
         constexpr int VEC = 16 / (int)sizeof(T);
         const int64_t i0 = st_.h_item[b], i1 = st_.h_item[b + 1];
@@ -1628,7 +2113,7 @@ struct Trainer {
 
     // true when the whole epoch ran as one persistent launch
     bool launch_epoch(const FwdArgs<T>& base) {
-        if (model != M_FM || n_streams != 1 || !coop) return false;
+        if (model != M_FM || n_streams != 1 || !coop || S[0].tab) return false;
         constexpr int VW = 16 / (int)sizeof(T);
         if (!multiclass && k % VW == 0 && k / VW <= 8) {
             const int nvec = (int)(k / VW);
@@ -1678,6 +2163,13 @@ struct Trainer {
                 A.order = p_order + e * n_rows;
                 A.pos0 = pos0;
                 A.nrows = nrows;
+                if (S[0].tab) {  // rows by epoch position
+                    A.indptr = S[0].estart.ptr;
+                    A.indices = reinterpret_cast<const int32_t*>(S[0].pidx.ptr);
+                    A.data = S[0].ex.ptr;
+                    A.y = S[0].py.ptr;
+                    A.sw = S[0].psw.ptr;
+                }
                 A.estart1 = S[0].estart.ptr;
                 A.seg1 = S[0].h_seg[b];
                 A.pay1 = S[0].pay.ptr;
@@ -1691,6 +2183,10 @@ struct Trainer {
                     A.inv2 = S[1].inv.ptr;
                 }
                 launch_forward(A, nrows);
+                if (S[0].tab) {
+                    launch_tab(b, inv_bsz, nrows);
+                    continue;
+                }
                 for (int si = 0; si < n_streams; ++si)
                     launch_reduce(S[si], b, inv_bsz, nrows, si == n_streams - 1);
             }

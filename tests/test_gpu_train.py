@@ -215,3 +215,66 @@ def test_device_resident_fit_matches_host_fit(dtype, opt):
     np.testing.assert_array_equal(V.cpu().numpy().astype(np.float64),
                                   host[2].astype(tdt == torch.float32 and np.float32
                                                  or np.float64).astype(np.float64))
+
+
+@pytest.mark.parametrize("opt", ["sgd", "adagrad", "adam", "ftrl"])
+def test_runs_across_many_chunks_f64(opt):
+    """Batches of 10,000 CTR-shaped rows: the 13 numeric features occur in
+    every row, so each of their runs spans 40 chunks of 256 sorted entries
+    (more chunk partials than one warp folds at once)."""
+    X, _ = workloads.ctr_fm(n_rows=20000, seed=5, space=2**16, vocab=2**12)
+    rng = np.random.default_rng(4)
+    y = (rng.random(X.n_rows) < 0.3).astype(np.float64)
+    sw = rng.uniform(0.5, 1.5, X.n_rows)
+    params = (0.0, np.zeros(X.n_features), rng.normal(0, 0.05, (X.n_features, 8)))
+    ro = workloads.row_orders(X.n_rows, 1, seed=2)
+    kw = dict(l1_linear=0.01, l1_factors=0.001) if opt == "ftrl" else {}
+    got = _fm_fit(_rust, X, y, sw, params, ro, 10000, True, optimizer=opt, **kw)
+    ref = _fm_fit(O, X, y, sw, params, ro, 10000, False, optimizer=opt, **kw)
+    keys = ("w0", "w", "V", "acc_w", "acc_V") if opt == "adagrad" else ("w0", "w", "V")
+    for g, r, key in zip(got, ref, keys):
+        _close(g, r, key)
+    if opt == "ftrl":
+        np.testing.assert_array_equal(got[1] == 0.0, ref[1] == 0.0)
+
+
+@pytest.mark.parametrize("opt", ["sgd", "adagrad"])
+def test_runs_across_many_chunks_f32(monkeypatch, opt):
+    """The 40-chunk runs in float32 (k=16, the row-table shape of the CTR
+    benchmark): weights within 1e-4 relative of the float64 oracle. (Adam is
+    held to the float64 bar above: its normalised first steps are +-lr for
+    any nonzero gradient, so float32 rounding of a near-zero gradient moves a
+    weight by up to lr.)"""
+    monkeypatch.setenv("MFM_B200_DTYPE", "float32")
+    X, _ = workloads.ctr_fm(n_rows=20000, seed=6, space=2**16, vocab=2**12)
+    rng = np.random.default_rng(5)
+    y = (rng.random(X.n_rows) < 0.3).astype(np.float64)
+    params = (0.0, np.zeros(X.n_features), rng.normal(0, 0.05, (X.n_features, 16)))
+    ro = workloads.row_orders(X.n_rows, 2, seed=3)
+    got = _fm_fit(_rust, X, y, np.ones(X.n_rows), params, ro, 10000, True, optimizer=opt)
+    ref = _fm_fit(O, X, y, np.ones(X.n_rows), params, ro, 10000, False, optimizer=opt)
+    for g, r, key in zip(got[:3], ref[:3], ("w0", "w", "V")):
+        scale = np.max(np.abs(r))
+        np.testing.assert_allclose(g, r, rtol=1e-4, atol=1e-4 * scale, err_msg=key)
+
+
+@pytest.mark.parametrize("k", [4, 8, 16])
+def test_single_feature_and_empty_batches(k):
+    """One feature (a single sort key, zero key bits), rows without nonzeros
+    and a batch made only of empty rows: w0 still steps every batch."""
+    n = 60
+    rng = np.random.default_rng(k)
+    nz = np.ones(n, dtype=np.int64)
+    nz[:10] = 0          # epoch 0, batch 0: all empty
+    nz[25:30] = 0
+    indptr = np.concatenate([[0], np.cumsum(nz)])
+    X = workloads.Csr(indptr, np.zeros(int(indptr[-1]), dtype=np.int64),
+                      rng.uniform(0.5, 2.0, int(indptr[-1])), 1)
+    y = (rng.random(n) < 0.5).astype(np.float64)
+    params = (0.2, np.array([0.1]), rng.normal(0, 0.1, (1, k)))
+    ro = np.stack([np.arange(n), rng.permutation(n)])
+    for opt in ("sgd", "adagrad", "adam", "ftrl"):
+        got = _fm_fit(_rust, X, y, np.ones(n), params, ro, 10, True, optimizer=opt)
+        ref = _fm_fit(O, X, y, np.ones(n), params, ro, 10, False, optimizer=opt)
+        for g, r, key in zip(got[:3], ref[:3], ("w0", "w", "V")):
+            _close(g, r, f"{opt} {key}")
