@@ -75,6 +75,10 @@ std::mutex& device_mutex(int device);
 int device_count();
 int sm_count(int device);
 
+// Per-device streams for work that runs beside the caller's stream: which = 0
+// has the device's greatest priority, which = 1 its least.
+cudaStream_t side_stream(int device, int which);
+
 // Caching allocator: freed blocks are kept per device and reused for
 // requests up to 2x smaller; on cudaMalloc failure the cache is released and
 // the allocation retried once.

@@ -65,6 +65,20 @@ cudaStream_t device_stream(int device) {
     return g_streams[device];
 }
 
+cudaStream_t side_stream(int device, int which) {
+    static cudaStream_t streams[kMaxDevices][2] = {};
+    std::lock_guard<std::mutex> lk(g_init_mu);
+    cudaStream_t& st = streams[device % kMaxDevices][which & 1];
+    if (!st) {
+        int least = 0, greatest = 0;
+        MFM_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+        MFM_CUDA(cudaStreamCreateWithPriority(&st, cudaStreamNonBlocking,
+                                              which == 0 ? greatest : least),
+                 "stream create");
+    }
+    return st;
+}
+
 int sm_count(int device) {
     if (!g_sms[device]) {
         int v = 0;

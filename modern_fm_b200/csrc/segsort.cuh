@@ -6,22 +6,25 @@
 //   2. seg_offsets_kernel: per segment, digit-major / tile-minor exclusive
 //                          prefix -> the output offset of every (tile, digit);
 //   3. seg_scatter_kernel: per tile, stable rank of each entry among equal
-//                          digits (warp match + per-warp counts) and scatter.
+//                          digits (warp match + per-warp counters, 16 keys per
+//                          thread) and scatter.
 // Stability makes the final order (key, original position) — deterministic,
 // with no floating point involved. The last pass can replace each value by
 // data gathered through it (RecGather): the sorted stream then carries what
 // its consumer reads instead of an index into the unsorted one.
 #pragma once
 
+#include <algorithm>
 #include <type_traits>
+#include <vector>
 
 #include "scan.cuh"
 
 namespace mfm {
 
-constexpr int kSortNT = 1024;
-constexpr int kSortRounds = 4;
-constexpr int kSortTile = kSortNT * kSortRounds;
+constexpr int kSortNT = 256;    // threads per tile (= digits per pass)
+constexpr int kSortItems = 16;  // keys per thread
+constexpr int kSortTile = kSortNT * kSortItems;
 
 __global__ void __launch_bounds__(256)
     seg_hist_kernel(const uint32_t* __restrict__ keys, const int64_t* __restrict__ tile_lo,
@@ -77,6 +80,13 @@ struct RecGather {
     }
 };
 
+// Per tile: 256 threads x 16 keys in a striped layout (item i of lane l in
+// warp w sits at tile start + w*512 + i*32 + l, so a warp's items in item
+// order are in position order). Each warp ranks its keys among equal digits
+// with match_any and per-warp digit counters; a prefix over the warps per
+// digit and over the digits gives each key its stable tile-local position.
+// The tile is reordered by digit in shared memory, then written out: every
+// digit's keys form one contiguous run of the output, so the stores coalesce.
 template <class Out>
 __global__ void __launch_bounds__(kSortNT)
     seg_scatter_kernel(const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin,
@@ -84,49 +94,71 @@ __global__ void __launch_bounds__(kSortNT)
                        const int64_t* __restrict__ tile_lo, const int64_t* __restrict__ tile_hi,
                        const int64_t* __restrict__ tile_seg_lo, int shift,
                        const uint32_t* __restrict__ offs, Out out) {
-    __shared__ uint32_t wh[kSortNT / 32][256];  // per-warp digit counts -> prefixes
-    __shared__ uint32_t running[256];
-    __shared__ uint32_t round_tot[256];
+    constexpr int NW = kSortNT / 32;
+    __shared__ uint32_t cnt[NW][256];  // per-warp digit counts -> tile-local start per warp
+    __shared__ uint32_t base[256];     // output offset (segment-relative) minus tile-local start
+    __shared__ uint32_t scan_sm[NW];
+    __shared__ uint32_t skey[kSortTile], sval[kSortTile];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t lo = tile_lo[blockIdx.x], hi = tile_hi[blockIdx.x];
     const int64_t seg0 = tile_seg_lo[blockIdx.x];
-    if (t < 256) running[t] = offs[(int64_t)blockIdx.x * 256 + t];
+    for (int i = t; i < NW * 256; i += kSortNT) (&cnt[0][0])[i] = 0;
+    const uint32_t goff = offs[(int64_t)blockIdx.x * 256 + t];
+    const int n = (int)(hi - lo), q0 = warp * (32 * kSortItems) + lane;  // tile-local
+    const uint32_t* kt = kin + lo;
+    const uint32_t* vt = vin + lo;
+    uint32_t key[kSortItems], val[kSortItems], rank[kSortItems];
+#pragma unroll
+    for (int i = 0; i < kSortItems; ++i) {
+        const int q = q0 + i * 32;
+        key[i] = q < n ? kt[q] : 0u;
+        val[i] = q < n ? vt[q] : 0u;
+    }
+    __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
-    for (int r = 0; r < kSortRounds; ++r) {
-        const int64_t p = lo + (int64_t)r * kSortNT + t;
-        const bool valid = p < hi;
-        if (lo + (int64_t)r * kSortNT >= hi) break;  // uniform across the block
-        uint32_t key = 0, val = 0;
-        if (valid) {
-            key = kin[p];
-            val = vin[p];
-        }
-        const uint32_t d = valid ? (key >> shift) & 255u : 256u + (uint32_t)lane;
-        for (int i = t; i < (kSortNT / 32) * 256; i += kSortNT) (&wh[0][0])[i] = 0;
-        __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kSortItems; ++i) {
+        const bool valid = q0 + i * 32 < n;
+        const uint32_t d = valid ? (key[i] >> shift) & 255u : 256u + (uint32_t)lane;
         const unsigned peers = __match_any_sync(0xffffffffu, d);
-        const int rank = __popc(peers & lt);
-        if (valid && rank == 0) wh[warp][d] = (uint32_t)__popc(peers);
-        __syncthreads();
-        if (t < 256) {
-            uint32_t acc = 0;
-#pragma unroll 8
-            for (int w = 0; w < kSortNT / 32; ++w) {
-                const uint32_t c = wh[w][t];
-                wh[w][t] = acc;
-                acc += c;
-            }
-            round_tot[t] = acc;
+        const int leader = __ffs(peers) - 1;
+        uint32_t b = 0;
+        if (valid && lane == leader) {
+            b = cnt[warp][d];
+            cnt[warp][d] = b + (uint32_t)__popc(peers);
         }
-        __syncthreads();
-        if (valid) {
-            const int64_t dst = seg0 + running[d] + wh[warp][d] + rank;
-            kout[dst] = key;
-            out(vout, dst, seg0, val);
+        b = __shfl_sync(0xffffffffu, b, leader);
+        rank[i] = b + (uint32_t)__popc(peers & lt);
+        __syncwarp();  // this item's counter update before the next item's read
+    }
+    __syncthreads();
+    uint32_t tot = 0;  // thread t = digit t: prefix over the warps, then over the digits
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const uint32_t c = cnt[w][t];
+        cnt[w][t] = tot;
+        tot += c;
+    }
+    uint32_t all;
+    const uint32_t dstart = block_exclusive_scan<uint32_t, kSortNT>(tot, scan_sm, all);
+#pragma unroll
+    for (int w = 0; w < NW; ++w) cnt[w][t] += dstart;
+    base[t] = goff - dstart;
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kSortItems; ++i)
+        if (q0 + i * 32 < n) {
+            const uint32_t d = (key[i] >> shift) & 255u;
+            const uint32_t lp = cnt[warp][d] + rank[i];
+            skey[lp] = key[i];
+            sval[lp] = val[i];
         }
-        __syncthreads();
-        if (t < 256) running[t] += round_tot[t];
-        __syncthreads();
+    __syncthreads();
+    for (int j = t; j < n; j += kSortNT) {
+        const uint32_t k = skey[j];
+        const int64_t dst = seg0 + (int64_t)(base[(k >> shift) & 255u] + (uint32_t)j);
+        kout[dst] = k;
+        out(vout, dst, seg0, sval[j]);
     }
 }
 
@@ -205,6 +237,90 @@ SortResult segmented_sort(int device, cudaStream_t s, uint32_t* k0, uint32_t* v0
         vi = vo;
         ko = nk;
         vo = nv;
+    }
+    res.keys = const_cast<uint32_t*>(ki);
+    res.vals = vi;
+    return res;
+}
+
+// The tile table of a whole epoch, built on the host from the segment
+// bounds, so that sorting a range of segments needs no host round trip.
+struct SortTiles {
+    DevBuf<int64_t> seg_tile, tlo, thi, tseg;  // seg_tile: first tile of each segment (n_seg + 1)
+    DevBuf<uint32_t> hist;                    // 256 counters / offsets per tile
+    std::vector<int64_t> h_seg_tile;
+    int64_t n_tiles = 0;
+};
+
+inline void build_sort_tiles(int device, cudaStream_t s, const std::vector<int64_t>& h_seg,
+                             int64_t n_seg, SortTiles& T) {
+    T.h_seg_tile.assign(n_seg + 1, 0);
+    for (int64_t b = 0; b < n_seg; ++b)
+        T.h_seg_tile[b + 1] = T.h_seg_tile[b] + ceil_div(h_seg[b + 1] - h_seg[b], kSortTile);
+    T.n_tiles = T.h_seg_tile[n_seg];
+    std::vector<int64_t> lo(T.n_tiles), hi(T.n_tiles), sg(T.n_tiles);
+    for (int64_t b = 0; b < n_seg; ++b) {
+        int64_t t = T.h_seg_tile[b];
+        for (int64_t p = h_seg[b]; p < h_seg[b + 1]; p += kSortTile, ++t) {
+            lo[t] = p;
+            hi[t] = std::min<int64_t>(p + kSortTile, h_seg[b + 1]);
+            sg[t] = h_seg[b];
+        }
+    }
+    T.seg_tile.alloc(device, n_seg + 1);
+    h2d(T.seg_tile.ptr, T.h_seg_tile.data(), n_seg + 1, s, "sort tiles");
+    const int64_t nt = std::max<int64_t>(T.n_tiles, 1);
+    T.tlo.alloc(device, nt);
+    T.thi.alloc(device, nt);
+    T.tseg.alloc(device, nt);
+    T.hist.alloc(device, (size_t)nt * 256);
+    if (T.n_tiles > 0) {
+        h2d(T.tlo.ptr, lo.data(), T.n_tiles, s, "sort tiles");
+        h2d(T.thi.ptr, hi.data(), T.n_tiles, s, "sort tiles");
+        h2d(T.tseg.ptr, sg.data(), T.n_tiles, s, "sort tiles");
+    }
+    MFM_CUDA(cudaStreamSynchronize(s), "sort tiles");  // the host vectors go out of scope
+}
+
+// segmented_sort restricted to segments [b0, b1) with the epoch tile table T;
+// no host synchronisation. Same buffer rules as segmented_sort.
+template <class Last = PlainValue>
+SortResult segmented_sort_range(cudaStream_t s, const uint32_t* kfirst, uint32_t* k0, uint32_t* v0,
+                                uint32_t* k1, uint32_t* v1, const int64_t* d_seg_lo, int64_t b0,
+                                int64_t b1, SortTiles& T, int key_bits, Last last = Last{}) {
+    SortResult res{k0, v0};
+    constexpr bool gather = !std::is_same<Last, PlainValue>::value;
+    if (gather && key_bits < 1) key_bits = 1;
+    const int64_t t0 = T.h_seg_tile[b0], t1 = T.h_seg_tile[b1];
+    const uint32_t* ki = kfirst ? kfirst : k0;
+    uint32_t *vi = v0, *ko = k1, *vo = v1;
+    if (t1 > t0 && key_bits > 0) {
+        const unsigned nt = (unsigned)(t1 - t0), ns = (unsigned)(b1 - b0);
+        const int64_t* tlo = T.tlo.ptr + t0;
+        const int64_t* thi = T.thi.ptr + t0;
+        const int64_t* tsg = T.tseg.ptr + t0;
+        uint32_t* hist = T.hist.ptr + t0 * 256;
+        for (int shift = 0; shift < key_bits; shift += 8) {
+            seg_hist_kernel<<<nt, 256, 0, s>>>(ki, tlo, thi, shift, hist);
+            seg_offsets_kernel<<<ns, 256, 0, s>>>(d_seg_lo + b0, T.seg_tile.ptr + b0, T.hist.ptr);
+            if (gather && shift + 8 >= key_bits)
+                seg_scatter_kernel<Last><<<nt, kSortNT, 0, s>>>(ki, vi, ko, vo, tlo, thi, tsg,
+                                                                shift, hist, last);
+            else
+                seg_scatter_kernel<PlainValue><<<nt, kSortNT, 0, s>>>(
+                    ki, vi, ko, vo, tlo, thi, tsg, shift, hist, PlainValue{});
+            MFM_CHECK_LAUNCH("segmented sort launch");
+            uint32_t* nk = ko == k1 ? k0 : k1;
+            uint32_t* nv = vo == v1 ? v0 : v1;
+            ki = ko;
+            vi = vo;
+            ko = nk;
+            vo = nv;
+        }
+    } else if (key_bits > 0) {  // no entries: report where a sort would have ended
+        const int passes = (key_bits + 7) / 8;
+        ki = passes % 2 ? k1 : k0;
+        vi = passes % 2 ? v1 : v0;
     }
     res.keys = const_cast<uint32_t*>(ki);
     res.vals = vi;

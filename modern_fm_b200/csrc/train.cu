@@ -299,15 +299,15 @@ template <class T>
 __global__ void __launch_bounds__(256)
     expand_kernel(int kind, const int32_t* __restrict__ order, const int64_t* __restrict__ indptr,
                   const int32_t* __restrict__ indices, const int32_t* __restrict__ fid, int F,
-                  int64_t n_rows, int64_t B, const int64_t* __restrict__ estart,
+                  int64_t pos_lo, int64_t pos_hi, int64_t B, const int64_t* __restrict__ estart,
                   const int64_t* __restrict__ seg_lo, uint32_t* __restrict__ keys,
                   uint32_t* __restrict__ vals, const T* __restrict__ data,
                   uint32_t* __restrict__ erow, T* __restrict__ ex) {
     // (FEAT with erow: keys[] is kept unsorted as the epoch-order CSR indices)
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t pos = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; pos < n_rows;
-         pos += nwarps) {
+    for (int64_t pos = pos_lo + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+         pos < pos_hi; pos += nwarps) {
         const int64_t row = order[pos];
         const int64_t rb = indptr[row], z = indptr[row + 1] - rb;
         const int32_t* ix = indices + rb;
@@ -1168,7 +1168,7 @@ struct TabArgs {
 // float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
 template <class T, int NV, int OPT>
 constexpr int tab_min_blocks() {
-    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 4 : 1;
+    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 5 : 1;
 }
 
 template <class T, int VEC, int NV, int OPT>
@@ -1549,6 +1549,29 @@ int bits_for(int64_t n_keys) {
     return b;
 }
 
+struct Events {
+    std::vector<cudaEvent_t> e;
+    explicit Events(size_t n) : e(n, nullptr) {
+        for (auto& x : e) MFM_CUDA(cudaEventCreateWithFlags(&x, cudaEventDisableTiming), "event");
+    }
+    ~Events() {
+        for (auto x : e)
+            if (x) cudaEventDestroy(x);
+    }
+    Events(const Events&) = delete;
+    Events& operator=(const Events&) = delete;
+};
+
+// Batches per plan window of the row-table path (MFM_B200_PLAN_WINDOW).
+inline int64_t plan_window() {
+    static const int64_t w = [] {
+        const char* e = getenv("MFM_B200_PLAN_WINDOW");
+        const long long v = e ? atoll(e) : 0;
+        return v > 0 ? (int64_t)v : (int64_t)32;
+    }();
+    return w;
+}
+
 template <class T>
 struct Stream {
     int kind = FEAT;
@@ -1571,6 +1594,7 @@ struct Stream {
     DevBuf<uint32_t> erow, pidx;  // pidx: keys in epoch entry order (CSR indices by position)
     DevBuf<T> ex, rx, table, ph, pt, py, psw;
     uint32_t* rrow = nullptr;
+    SortTiles tiles;
 };
 
 template <class T>
@@ -1665,6 +1689,76 @@ struct Trainer {
         }
     }
 
+    // Row-table path, epoch-wide part (stream s): entry counts and starts,
+    // batch bounds (host copy), epoch-order labels, buffers and the sort's
+    // tile table. The per-window part (plan_tab_window) needs no host sync.
+    void plan_tab_epoch(Stream<T>& st_, int e) {
+        const int32_t* order = p_order + (int64_t)e * n_rows;
+        {
+            DevBuf<int64_t> cnt(device, n_rows);
+            st_.estart.alloc(device, n_rows + 1);
+            count_kernel<<<blocks_for(n_rows, 256), 256, 0, s>>>(FEAT, order, p_indptr, n_rows,
+                                                               cnt.ptr);
+            exclusive_scan<int64_t, int64_t>(device, s, cnt.ptr, n_rows, st_.estart.ptr);
+            st_.seg_lo.alloc(device, nb + 1);
+            seg_lo_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(st_.estart.ptr, n_rows, B, nb,
+                                                                st_.seg_lo.ptr);
+            st_.h_seg.resize(nb + 1);
+            d2h(st_.h_seg.data(), st_.seg_lo.ptr, nb + 1, s, "plan download");
+            MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        }
+        const int64_t N = st_.h_seg[nb];
+        st_.max_entries = 0;
+        for (int64_t b = 0; b < nb; ++b) {
+            const int64_t len = st_.h_seg[b + 1] - st_.h_seg[b];
+            if (len >= ((int64_t)1 << 32))
+                fail(MFM_ERR_UNSUPPORTED, "a batch has 2^32 or more gradient entries");
+            st_.max_entries = std::max(st_.max_entries, len);
+        }
+        const int64_t N1 = std::max<int64_t>(N, 1);
+        if (st_.k0.n < (size_t)N1 || !st_.k0.ptr) {
+            st_.k0.alloc(device, N1);
+            st_.v0.alloc(device, N1);
+            st_.k1.alloc(device, N1);
+            st_.v1.alloc(device, N1);
+            st_.erow.alloc(device, N1);
+            st_.pidx.alloc(device, N1);
+            st_.ex.alloc(device, N1);
+            st_.rx.alloc(device, N1);
+        }
+        if (st_.py.n < (size_t)n_rows || !st_.py.ptr) {
+            st_.py.alloc(device, n_rows);
+            st_.psw.alloc(device, n_rows);
+        }
+        permute_rows_kernel<T><<<blocks_for(n_rows, 256), 256, 0, s>>>(
+            order, p_y, p_sw, n_rows, st_.py.ptr, st_.psw.ptr);
+        MFM_CHECK_LAUNCH("plan");
+        const int64_t mc = std::max<int64_t>(1, ceil_div(st_.max_entries, kChunk));
+        if (st_.ph.n < (size_t)(mc * st_.TW) || !st_.ph.ptr) {
+            st_.ph.alloc(device, mc * st_.TW);
+            st_.pt.alloc(device, mc * st_.TW);
+        }
+        build_sort_tiles(device, s, st_.h_seg, nb, st_.tiles);  // synchronises s
+    }
+
+    // Row-table path, batches [b0, b1) of epoch e on stream ps: epoch-order
+    // CSR entries (pidx, ex) and the sorted (key, row, x) stream.
+    void plan_tab_window(Stream<T>& st_, int e, int64_t b0, int64_t b1, cudaStream_t ps) {
+        const int32_t* order = p_order + (int64_t)e * n_rows;
+        const int64_t p0 = b0 * B, p1 = std::min(b1 * B, n_rows);
+        if (p1 > p0)
+            expand_kernel<T><<<warp_grid(device, p1 - p0, 8, 8), 256, 0, ps>>>(
+                FEAT, order, p_indptr, p_indices, p_fid, (int)F, p0, p1, B, st_.estart.ptr,
+                st_.seg_lo.ptr, st_.pidx.ptr, st_.v0.ptr, p_data, st_.erow.ptr, st_.ex.ptr);
+        MFM_CHECK_LAUNCH("expand");
+        SortResult sr = segmented_sort_range(
+            ps, st_.pidx.ptr, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr, st_.seg_lo.ptr, b0,
+            b1, st_.tiles, bits_for(st_.n_keys),
+            RecGather<T>{st_.erow.ptr, st_.ex.ptr, st_.rx.ptr});
+        st_.keys = sr.keys;  // the same buffers for every window
+        st_.rrow = sr.vals;
+    }
+
     // count -> scan -> expand -> segmented sort -> runs -> items, for epoch e
     void plan(Stream<T>& st_, int e) {
         const int32_t* order = p_order + (int64_t)e * n_rows;
@@ -1693,41 +1787,11 @@ struct Trainer {
             st_.k1.alloc(device, N);
             st_.v1.alloc(device, N);
         }
-        if (st_.tab && (st_.erow.n < (size_t)N || !st_.erow.ptr)) {
-            st_.erow.alloc(device, std::max<int64_t>(N, 1));
-            st_.pidx.alloc(device, std::max<int64_t>(N, 1));
-            st_.ex.alloc(device, std::max<int64_t>(N, 1));
-            st_.rx.alloc(device, std::max<int64_t>(N, 1));
-        }
         expand_kernel<T><<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
-            st_.kind, order, p_indptr, p_indices, p_fid, (int)F, n_rows, B,
-            st_.estart.ptr, st_.seg_lo.ptr, st_.tab ? st_.pidx.ptr : st_.k0.ptr, st_.v0.ptr,
-            p_data, st_.tab ? st_.erow.ptr : nullptr, st_.tab ? st_.ex.ptr : nullptr);
+            st_.kind, order, p_indptr, p_indices, p_fid, (int)F, 0, n_rows, B,
+            st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr, p_data, nullptr,
+            static_cast<T*>(nullptr));
         MFM_CHECK_LAUNCH("expand");
-        if (st_.tab) {
-            // epoch-order CSR (estart, pidx, ex) + labels for the forward; sorted
-            // (key, row, x) for the reduction; chunk partials for the largest batch
-            if (st_.py.n < (size_t)n_rows || !st_.py.ptr) {
-                st_.py.alloc(device, n_rows);
-                st_.psw.alloc(device, n_rows);
-            }
-            permute_rows_kernel<T><<<blocks_for(n_rows, 256), 256, 0, s>>>(
-                order, p_y, p_sw, n_rows, st_.py.ptr, st_.psw.ptr);
-            SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr,
-                                           st_.v1.ptr, st_.seg_lo.ptr, nb, N,
-                                           bits_for(st_.n_keys),
-                                           RecGather<T>{st_.erow.ptr, st_.ex.ptr, st_.rx.ptr},
-                                           st_.pidx.ptr);
-            st_.keys = sr.keys;
-            st_.rrow = sr.vals;
-            const int64_t mc = std::max<int64_t>(1, ceil_div(st_.max_entries, kChunk));
-            if (st_.ph.n < (size_t)(mc * st_.TW) || !st_.ph.ptr) {
-                st_.ph.alloc(device, mc * st_.TW);
-                st_.pt.alloc(device, mc * st_.TW);
-            }
-            MFM_CHECK_LAUNCH("plan");
-            return;
-        }
         SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr,
                                        st_.seg_lo.ptr, nb, N, bits_for(st_.n_keys));
         st_.keys = sr.keys;
@@ -2140,7 +2204,83 @@ struct Trainer {
         return true;
     }
 
+    // Row-table path: each epoch's plan runs in windows of batches (one event
+    // per window) on the plan stream, the batches on a high-priority stream
+    // forked from and joined back to s.
+    void run_tab(const FwdArgs<T>& base, PhaseTimer& pt) {
+        const cudaStream_t caller = s;
+        // MFM_B200_PLAN_OVERLAP=1 runs the plan in windows on a second stream
+        // beside the batches; by default it is one window that precedes the
+        // batches on one stream (the sort's blocks fill every SM, so
+        // overlapping only delays the latency-bound batch kernels).
+        const char* ov = getenv("MFM_B200_PLAN_OVERLAP");
+        const bool overlap = ov && *ov == '1';
+        const cudaStream_t hi = side_stream(device, 0);
+        const cudaStream_t lo = overlap ? side_stream(device, 1) : hi;
+        std::vector<std::pair<int64_t, int64_t>> win;
+        for (int64_t b0 = 0, w = 0; b0 < nb; ++w) {  // 4, 8, 16, then plan_window() batches
+            const int64_t len = !overlap ? nb
+                                         : std::min<int64_t>(plan_window(),
+                                                             (int64_t)4 << std::min<int64_t>(w, 20));
+            const int64_t b1 = std::min(nb, b0 + len);
+            win.emplace_back(b0, b1);
+            b0 = b1;
+        }
+        Events ev(win.size() + 3);
+        cudaEvent_t ev_fork = ev.e[win.size()], ev_ep = ev.e[win.size() + 1],
+                    ev_join = ev.e[win.size() + 2];
+        MFM_CUDA(cudaEventRecord(ev_fork, caller), "event");
+        MFM_CUDA(cudaStreamWaitEvent(hi, ev_fork, 0), "event");
+        s = hi;
+        pt.s = hi;
+        try {
+            for (int64_t e = 0; e < E; ++e) {
+                plan_tab_epoch(S[0], (int)e);
+                pt.mark("plan");
+                MFM_CUDA(cudaEventRecord(ev_ep, hi), "event");
+                MFM_CUDA(cudaStreamWaitEvent(lo, ev_ep, 0), "event");
+                for (size_t w = 0; w < win.size(); ++w) {
+                    plan_tab_window(S[0], (int)e, win[w].first, win[w].second, lo);
+                    MFM_CUDA(cudaEventRecord(ev.e[w], lo), "event");
+                }
+                for (size_t w = 0; w < win.size(); ++w) {
+                    MFM_CUDA(cudaStreamWaitEvent(hi, ev.e[w], 0), "event");
+                    for (int64_t b = win[w].first; b < win[w].second; ++b) {
+                        const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
+                        const T inv_bsz = T(1) / (T)nrows;  // batch length (fm.rs:395-398)
+                        FwdArgs<T> A = base;
+                        A.pos0 = pos0;
+                        A.nrows = nrows;
+                        A.indptr = S[0].estart.ptr;  // rows by epoch position
+                        A.indices = reinterpret_cast<const int32_t*>(S[0].pidx.ptr);
+                        A.data = S[0].ex.ptr;
+                        A.y = S[0].py.ptr;
+                        A.sw = S[0].psw.ptr;
+                        launch_forward(A, nrows);
+                        launch_tab(b, inv_bsz, nrows);
+                    }
+                }
+                pt.mark("batches");
+            }
+        } catch (...) {
+            cudaStreamSynchronize(lo);  // no kernel may outlive the buffers
+            cudaStreamSynchronize(hi);
+            s = caller;
+            pt.s = caller;
+            throw;
+        }
+        MFM_CUDA(cudaEventRecord(ev_join, hi), "event");
+        MFM_CUDA(cudaStreamWaitEvent(caller, ev_join, 0), "event");
+        s = caller;
+        pt.s = caller;
+        MFM_CUDA(cudaStreamSynchronize(s), "training");
+    }
+
     void run(const FwdArgs<T>& base, PhaseTimer& pt) {
+        if (S[0].tab) {
+            run_tab(base, pt);
+            return;
+        }
         for (int64_t e = 0; e < E; ++e) {
             for (int si = 0; si < n_streams; ++si) plan(S[si], (int)e);
             pt.mark("plan");
@@ -2163,13 +2303,6 @@ struct Trainer {
                 A.order = p_order + e * n_rows;
                 A.pos0 = pos0;
                 A.nrows = nrows;
-                if (S[0].tab) {  // rows by epoch position
-                    A.indptr = S[0].estart.ptr;
-                    A.indices = reinterpret_cast<const int32_t*>(S[0].pidx.ptr);
-                    A.data = S[0].ex.ptr;
-                    A.y = S[0].py.ptr;
-                    A.sw = S[0].psw.ptr;
-                }
                 A.estart1 = S[0].estart.ptr;
                 A.seg1 = S[0].h_seg[b];
                 A.pay1 = S[0].pay.ptr;
@@ -2183,10 +2316,6 @@ struct Trainer {
                     A.inv2 = S[1].inv.ptr;
                 }
                 launch_forward(A, nrows);
-                if (S[0].tab) {
-                    launch_tab(b, inv_bsz, nrows);
-                    continue;
-                }
                 for (int si = 0; si < n_streams; ++si)
                     launch_reduce(S[si], b, inv_bsz, nrows, si == n_streams - 1);
             }
