@@ -31,6 +31,7 @@
 //       fixed order and applies; its last block steps w0 from the per-row
 //       gradients.
 #include <algorithm>
+#include <mutex>
 #include <utility>
 #include <cmath>
 
@@ -1146,7 +1147,7 @@ __global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t 
 // pt[first chunk] + ph[...] in chunk order and applies; the last block steps
 // w0. Every sum has a fixed shape, so results are bitwise reproducible.
 
-constexpr int kChunk = 256;
+constexpr int kChunk = 256;  // sorted entries per stage-1 block
 
 template <class T>
 struct TabArgs {
@@ -1168,7 +1169,7 @@ struct TabArgs {
 // float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
 template <class T, int NV, int OPT>
 constexpr int tab_min_blocks() {
-    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 5 : 1;
+    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 4 : 1;
 }
 
 template <class T, int VEC, int NV, int OPT>
@@ -1224,9 +1225,11 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
 #pragma unroll
         for (int q = 0; q < NVAL; ++q) val[q] = T(0);
     }
-    // segmented suffix sums: lane l ends with the sum over [l, send]
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
+    // segmented suffix sums: lane l ends with the sum over [l, send]; steps
+    // beyond the warp's longest segment add nothing and are skipped
+    const int seglen = (rhead || lane == 0) ? send - lane + 1 : 1;
+    const int maxlen = (int)__reduce_max_sync(FULL, (unsigned)seglen);
+    for (int o = 1; o < maxlen; o <<= 1) {
         const bool take = lane + o <= send;
 #pragma unroll
         for (int q = 0; q < NVAL; ++q) {
