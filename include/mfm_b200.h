@@ -234,6 +234,34 @@ int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr, const int32_
                       const mfm_train* tr, int64_t k, mfm_dev_group* w0, mfm_dev_group* w,
                       mfm_dev_group* v, void* stream);
 
+/* ---- data-parallel training (no reference counterpart) -------------------
+ * Synchronous data parallelism over NCCL (NVLink / NVSwitch): every rank holds
+ * the whole training set, the parameters and the optimizer state; each global
+ * batch (the same row_orders chunking as one GPU) is cut into `world`
+ * contiguous row slices, rank r scores slice r, the per-key gradient sums over
+ * the batch's sorted union of touched keys are summed across ranks with one
+ * ncclAllReduce, and every rank applies the identical optimizer step. NCCL is
+ * loaded on first use (dlopen "libnccl.so.2").
+ *   mfm_dp_unique_id: rank 0 makes the group id (128 bytes) and the caller
+ *     hands it to every rank;
+ *   mfm_dp_create: every rank, concurrently; binds the group to `device`;
+ *   mfm_dp_destroy: after the last fit. */
+typedef struct mfm_dp mfm_dp;
+int mfm_dp_unique_id(unsigned char id[128]);
+int mfm_dp_create(const unsigned char id[128], int world, int rank, int device, mfm_dp** out);
+int mfm_dp_destroy(mfm_dp* dp);
+
+/* mfm_fm_fit_device across the group (same arguments; the device is the
+ * group's). Binary FM with k = 4, 8, 16, 32 (float32) or 2, 4, 8, 16
+ * (float64); other shapes return MFM_ERR_UNSUPPORTED. Every rank must call it
+ * with the same data, row orders and hyperparameters; results are identical
+ * on every rank. */
+int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr, const int32_t* indices,
+                         const void* data, int64_t n_rows, int64_t n_features, const void* y,
+                         const void* sample_weight, const int32_t* row_orders,
+                         const mfm_train* tr, int64_t k, mfm_dev_group* w0, mfm_dev_group* w,
+                         mfm_dev_group* v, void* stream);
+
 /* Release the engine's cached device memory on every device. */
 void mfm_release_cached_memory(void);
 

@@ -14,6 +14,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libmfm_b200.so")
 
 MFM_OK = 0
+MFM_ERR_INVALID, MFM_ERR_UNSUPPORTED = -1, -2
 MFM_DTYPE_F64, MFM_DTYPE_F32 = 0, 1
 LOSSES = {"logistic": 0, "squared": 1}
 OPTIMIZERS = {"sgd": 0, "adagrad": 1, "adam": 2, "ftrl": 3}
@@ -82,6 +83,14 @@ _SIGNATURES = {
                                      ct.c_int64, ct.c_int64, ct.c_void_p, ct.c_void_p,
                                      ct.c_void_p, ct.POINTER(Train), ct.c_int64]
                           + [ct.POINTER(DevGroup)] * 3 + [ct.c_void_p]),
+    "mfm_dp_unique_id": (ct.c_int, [ct.c_char_p]),
+    "mfm_dp_create": (ct.c_int, [ct.c_char_p, ct.c_int, ct.c_int, ct.c_int,
+                                 ct.POINTER(ct.c_void_p)]),
+    "mfm_dp_destroy": (ct.c_int, [ct.c_void_p]),
+    "mfm_fm_fit_device_dp": (ct.c_int, [ct.c_void_p, ct.c_int, ct.c_void_p, ct.c_void_p,
+                                        ct.c_void_p, ct.c_int64, ct.c_int64, ct.c_void_p,
+                                        ct.c_void_p, ct.c_void_p, ct.POINTER(Train), ct.c_int64]
+                             + [ct.POINTER(DevGroup)] * 3 + [ct.c_void_p]),
     "mfm_fm_predict_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_double, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]),

@@ -31,11 +31,20 @@
 //       fixed order and applies; its last block steps w0 from the per-row
 //       gradients.
 #include <algorithm>
+#include <cstring>
+#include <dlfcn.h>
+#include <nccl.h>
 #include <mutex>
 #include <utility>
 #include <cmath>
 
 #include "segsort.cuh"
+
+// A data-parallel group: one NCCL communicator bound to a device.
+struct mfm_dp {
+    ncclComm_t comm;
+    int world, rank, device;
+};
 
 namespace mfm {
 
@@ -425,6 +434,20 @@ __global__ void batch_tables_kernel(const int64_t* __restrict__ seg_lo, int64_t 
     const int64_t r = run_id[seg_lo[b]];
     bitem[b] = item_start[r];
     blong[b] = long_scan[r];
+}
+
+// Data-parallel plan: key of each run (distinct key per batch) and the runs
+// before each batch.
+__global__ void run_key_kernel(const uint32_t* __restrict__ keys, const int32_t* __restrict__ head,
+                               const int64_t* __restrict__ runs, int64_t n,
+                               uint32_t* __restrict__ rkey) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && head[i]) rkey[runs[i]] = keys[i];
+}
+__global__ void batch_runs_kernel(const int64_t* __restrict__ seg_lo, int64_t nb,
+                                  const int64_t* __restrict__ runs, int64_t* __restrict__ brun) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b <= nb) brun[b] = runs[seg_lo[b]];
 }
 
 // ------------------------------------------------------ forward kernels --
@@ -1022,29 +1045,38 @@ __global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t
 // The last block steps w0 from the batch's per-row gradients (fixed tree).
 // w0: the batch's per-row gradients summed in a fixed tree by one block,
 // then one step per class (step_param with l1 = l2 = 0, optimizer.rs:114-135).
+// Sum of grow[j * C + c] over j < nrows in a fixed tree (valid in thread 0);
+// every thread of the block calls it.
+template <class T>
+__device__ __forceinline__ T block_sum_rows(const T* grow, int64_t nrows, int C, int c, T* sm) {
+    T s = T(0);
+    const int64_t bd = blockDim.x;
+    int64_t j = threadIdx.x;
+    for (; j + 7 * bd < nrows; j += 8 * bd) {  // eight loads in flight, same order
+        T a[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) a[u] = grow[(j + u * bd) * C + c];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) s += a[u];
+    }
+    for (; j < nrows; j += bd) s += grow[j * C + c];
+    sm[threadIdx.x] = s;
+    __syncthreads();
+    for (int h = blockDim.x / 2; h > 0; h >>= 1) {
+        if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
+        __syncthreads();
+    }
+    const T r = sm[0];
+    __syncthreads();
+    return r;
+}
+
 template <class T>
 __device__ __forceinline__ void w0_step_dev(const T* grow, int64_t nrows, int C, T inv_bsz,
                                             const GroupDev<T>& gw0, const OptDev& opt, T* sm) {
     for (int c = 0; c < C; ++c) {
-        T s = T(0);
-        const int64_t bd = blockDim.x;
-        int64_t j = threadIdx.x;
-        for (; j + 7 * bd < nrows; j += 8 * bd) {  // eight loads in flight, same order
-            T a[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) a[u] = grow[(j + u * bd) * C + c];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) s += a[u];
-        }
-        for (; j < nrows; j += bd) s += grow[j * C + c];
-        sm[threadIdx.x] = s;
-        __syncthreads();
-        for (int h = blockDim.x / 2; h > 0; h >>= 1) {
-            if (threadIdx.x < h) sm[threadIdx.x] += sm[threadIdx.x + h];
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) opt_step(gw0, c, sm[0] * inv_bsz, opt);
-        __syncthreads();
+        const T tot = block_sum_rows(grow, nrows, C, c, sm);
+        if (threadIdx.x == 0) opt_step(gw0, c, tot * inv_bsz, opt);
     }
 }
 
@@ -1164,6 +1196,16 @@ struct TabArgs {
     T inv_bsz;
     GroupDev<T> gv, gw, gw0;
     OptDev opt;
+    // data-parallel batch (dp != 0): this rank scores rows [rlo, rhi) of the
+    // batch; per-run sums go to grad (run - run0, stride TW; row nrun = w0)
+    // instead of the optimizer, which fm_tab_apply_kernel runs after the
+    // cross-rank sum
+    int dp;
+    uint32_t rlo, rhi;
+    const int64_t* runs;   // per sorted entry: runs (distinct keys) before it in the epoch
+    const uint32_t* rkey;  // key of each run of the epoch
+    int64_t run0, nrun;    // this batch's runs: [run0, run0 + nrun)
+    T* grad;
 };
 
 // float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
@@ -1209,7 +1251,9 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
 
     pdl_wait();  // the row table and the parameters are the predecessors' output
     T val[NVAL];
-    if (valid) {
+    // data-parallel: rows of other ranks' slices add nothing here
+    const bool mine = valid && (!A.dp || (row >= A.rlo && row < A.rhi));
+    if (mine) {
         const T* tr = A.tab + (int64_t)row * A.TW;
         const T* vp = A.gv.p + (int64_t)key * K;
         const T g = tr[K];
@@ -1272,6 +1316,18 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
         dst[K] = val[K];
         return;
     }
+    if (A.dp) {  // the run's sum for this rank, stepped after the cross-rank sum
+        T* gd = A.grad + (A.runs[gi] - A.run0) * A.TW;
+#pragma unroll
+        for (int v = 0; v < NV; ++v) {
+            Vec<T, VEC> o;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) o.v[u] = val[v * VEC + u];
+            *reinterpret_cast<Vec<T, VEC>*>(gd + v * VEC) = o;
+        }
+        gd[K] = val[K];
+        return;
+    }
     // the whole run lies in this chunk: one optimizer step per coordinate
     VecStep<T, VEC, OPT> st[NV];
     VecStep<T, 1, OPT> sw1;
@@ -1297,7 +1353,12 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
     if (blockIdx.x == gridDim.x - 1) {
         __shared__ T sm[256];
         pdl_wait();
-        w0_step_dev(A.grow, A.nrows, 1, A.inv_bsz, A.gw0, A.opt, sm);
+        if (!A.dp) {
+            w0_step_dev(A.grow, A.nrows, 1, A.inv_bsz, A.gw0, A.opt, sm);
+        } else {  // this rank's slice sum; stepped after the cross-rank sum
+            const T tot = block_sum_rows(A.grow + A.rlo, (int64_t)(A.rhi - A.rlo), 1, 0, sm);
+            if (threadIdx.x == 0) A.grad[A.nrun * A.TW] = tot;
+        }
         return;
     }
     const int lane = threadIdx.x & 31;
@@ -1337,10 +1398,12 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
     const int own = lane < NV ? lane : NV;  // column vector this lane applies (NV = w)
     VecStep<T, VEC> st;
     VecStep<T, 1> s1;
-    if (lane < NV)
-        st.prefetch(A.gv, (int64_t)key * K + lane * VEC, A.opt.kind);
-    else if (lane == NV)
-        s1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+    if (!A.dp) {
+        if (lane < NV)
+            st.prefetch(A.gv, (int64_t)key * K + lane * VEC, A.opt.kind);
+        else if (lane == NV)
+            s1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+    }
     T tot[K + 1];
 #pragma unroll
     for (int q = 0; q <= K; ++q) tot[q] = T(0);
@@ -1367,6 +1430,24 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
 #pragma unroll
         for (int q = 0; q <= K; ++q) tot[q] += part[q];
     }
+    if (A.dp) {  // the run's sum for this rank (its head entry lies before chunk c)
+        T* gd = A.grad + (A.runs[A.seg + c * kChunk] - 1 - A.run0) * A.TW;
+        if (lane < NV) {
+            Vec<T, VEC> o;
+#pragma unroll
+            for (int u = 0; u < VEC; ++u) {
+                T t = T(0);
+#pragma unroll
+                for (int v = 0; v < NV; ++v)
+                    if (v == own) t = tot[v * VEC + u];
+                o.v[u] = t;
+            }
+            *reinterpret_cast<Vec<T, VEC>*>(gd + lane * VEC) = o;
+        } else if (lane == NV) {
+            gd[K] = tot[K];
+        }
+        return;
+    }
     if (lane < NV) {
         T dg[VEC];
 #pragma unroll
@@ -1380,6 +1461,38 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
         st.commit(A.gv, (int64_t)key * K + lane * VEC, dg, A.opt);
     } else if (lane == NV) {
         const T dg = tot[K] * A.inv_bsz;
+        s1.commit(A.gw, (int64_t)key, &dg, A.opt);
+    }
+}
+
+// Data-parallel step: after the cross-rank sum of grad, one warp per run of
+// the batch applies the optimizer to its key (NV vector lanes + the w lane),
+// identically on every rank; thread 0 of block 0 also steps w0.
+template <class T, int VEC, int NV>
+__global__ void __launch_bounds__(256) fm_tab_apply_kernel(TabArgs<T> A) {
+    constexpr int K = VEC * NV;
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint32_t key = j < A.nrun ? A.rkey[A.run0 + j] : 0u;  // plan data
+    pdl_wait();  // grad is the cross-rank sum
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        opt_step(A.gw0, 0, A.grad[A.nrun * A.TW] * A.inv_bsz, A.opt);
+    if (j >= A.nrun) return;
+    const T* gd = A.grad + j * A.TW;
+    if (lane < NV) {
+        const int64_t idx0 = (int64_t)key * K + lane * VEC;
+        VecStep<T, VEC> st;
+        st.prefetch(A.gv, idx0, A.opt.kind);
+        const Vec<T, VEC> g = ldg_vec<T, VEC>(gd + lane * VEC);
+        T dg[VEC];
+#pragma unroll
+        for (int u = 0; u < VEC; ++u) dg[u] = g.v[u] * A.inv_bsz;
+        st.commit(A.gv, idx0, dg, A.opt);
+    } else if (lane == NV) {
+        VecStep<T, 1> s1;
+        s1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+        const T dg = gd[K] * A.inv_bsz;
         s1.commit(A.gw, (int64_t)key, &dg, A.opt);
     }
 }
@@ -1552,6 +1665,42 @@ int bits_for(int64_t n_keys) {
     return b;
 }
 
+// NCCL, loaded on first use (dlopen): a process that already holds a libnccl
+// (e.g. PyTorch's) resolves to it, others to the system library; the engine
+// never links NCCL, so single-GPU use does not depend on it.
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                              ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+inline const NcclApi& nccl() {
+    static const NcclApi api = [] {
+        NcclApi a;
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return a;
+        a.GetUniqueId = (decltype(a.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+        a.CommInitRank = (decltype(a.CommInitRank))dlsym(h, "ncclCommInitRank");
+        a.AllReduce = (decltype(a.AllReduce))dlsym(h, "ncclAllReduce");
+        a.CommDestroy = (decltype(a.CommDestroy))dlsym(h, "ncclCommDestroy");
+        a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
+        return a;
+    }();
+    if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.CommDestroy ||
+        !api.GetErrorString)
+        fail(MFM_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
+    return api;
+}
+#define MFM_NCCL(call, what)                                                          \
+    do {                                                                              \
+        const ncclResult_t r_ = (call);                                               \
+        if (r_ != ncclSuccess)                                                        \
+            fail(MFM_ERR_CUDA, fmt("%s: %s", what, nccl().GetErrorString(r_)));       \
+    } while (0)
+
 struct Events {
     std::vector<cudaEvent_t> e;
     explicit Events(size_t n) : e(n, nullptr) {
@@ -1598,6 +1747,13 @@ struct Stream {
     DevBuf<T> ex, rx, table, ph, pt, py, psw;
     uint32_t* rrow = nullptr;
     SortTiles tiles;
+    // data-parallel: runs (distinct keys per batch) of the sorted stream
+    DevBuf<int32_t> head;
+    DevBuf<int64_t> runs;     // per entry: runs before it in the epoch (N + 1)
+    DevBuf<uint32_t> rkey;    // key of each run
+    DevBuf<int64_t> brun;     // runs before each batch (nb + 1)
+    std::vector<int64_t> h_run;
+    DevBuf<T> grad;           // (max runs per batch + 1, TW)
 };
 
 template <class T>
@@ -1630,6 +1786,7 @@ struct Trainer {
     int n_streams = 1;
     DevBuf<GridBar> bar;
     bool coop = false;  // cooperative launches usable (persistent epoch loop)
+    mfm_dp* dp = nullptr;  // data-parallel group (row-table path only)
 
     void upload_group(int gi, const mfm_group* hg, int64_t R, int64_t K, int reg) {
         const int64_t n = (int64_t)C * R * K;
@@ -1760,6 +1917,35 @@ struct Trainer {
             RecGather<T>{st_.erow.ptr, st_.ex.ptr, st_.rx.ptr});
         st_.keys = sr.keys;  // the same buffers for every window
         st_.rrow = sr.vals;
+    }
+
+    // Data-parallel: runs of the sorted stream (every rank computes the same),
+    // their keys, and the runs before each batch (host copy).
+    void plan_tab_runs(Stream<T>& st_) {
+        const int64_t N = st_.h_seg[nb];
+        st_.head.alloc(device, std::max<int64_t>(N, 1));
+        st_.runs.alloc(device, N + 1);
+        if (N > 0) {
+            head_kernel<<<blocks_for(N, 256), 256, 0, s>>>(st_.keys, N, st_.head.ptr);
+            seg_head_kernel<<<blocks_for(nb, 256), 256, 0, s>>>(st_.seg_lo.ptr, nb, st_.head.ptr);
+        }
+        exclusive_scan<int32_t, int64_t>(device, s, st_.head.ptr, N, st_.runs.ptr);
+        st_.brun.alloc(device, nb + 1);
+        batch_runs_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(st_.seg_lo.ptr, nb,
+                                                                st_.runs.ptr, st_.brun.ptr);
+        st_.h_run.resize(nb + 1);
+        d2h(st_.h_run.data(), st_.brun.ptr, nb + 1, s, "plan download");
+        MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        const int64_t R = st_.h_run[nb];
+        st_.rkey.alloc(device, std::max<int64_t>(R, 1));
+        if (N > 0)
+            run_key_kernel<<<blocks_for(N, 256), 256, 0, s>>>(st_.keys, st_.head.ptr,
+                                                            st_.runs.ptr, N, st_.rkey.ptr);
+        int64_t mr = 0;
+        for (int64_t b = 0; b < nb; ++b) mr = std::max(mr, st_.h_run[b + 1] - st_.h_run[b]);
+        if (st_.grad.n < (size_t)((mr + 1) * st_.TW) || !st_.grad.ptr)
+            st_.grad.alloc(device, (mr + 1) * st_.TW);
+        MFM_CHECK_LAUNCH("plan");
     }
 
     // count -> scan -> expand -> segmented sort -> runs -> items, for epoch e
@@ -2091,9 +2277,19 @@ struct Trainer {
         const int64_t warps = std::max<int64_t>(0, nchunks - 1);
         launch_pdl(fm_tab_fold_kernel<T, VW, NV>, (unsigned)(ceil_div(warps, 8) + 1), 256, s, TA,
                    nchunks);
+        if (TA.dp) {  // cross-rank sum of the batch's run sums (+ w0), then the step
+            MFM_CHECK_LAUNCH("row-table reduction");
+            const size_t cnt = (size_t)(TA.nrun + 1) * TA.TW;
+            MFM_NCCL(nccl().AllReduce(TA.grad, TA.grad, cnt,
+                                      sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum,
+                                      dp->comm, s),
+                     "ncclAllReduce");
+            launch_pdl(fm_tab_apply_kernel<T, VW, NV>,
+                       (unsigned)std::max<int64_t>(1, ceil_div(TA.nrun, 8)), 256, s, TA);
+        }
         MFM_CHECK_LAUNCH("row-table reduction");
     }
-    void launch_tab(int64_t b, T inv_bsz, int64_t nrows) {
+    void launch_tab(int64_t b, T inv_bsz, int64_t nrows, int64_t rlo, int64_t rhi) {
         constexpr int VW = 16 / (int)sizeof(T);
         Stream<T>& st_ = S[0];
         TabArgs<T> TA;
@@ -2113,6 +2309,14 @@ struct Trainer {
         TA.gw = G[1];
         TA.gw0 = G[0];
         TA.opt = opt;
+        TA.dp = dp ? 1 : 0;
+        TA.rlo = (uint32_t)rlo;
+        TA.rhi = (uint32_t)rhi;
+        TA.runs = st_.runs.ptr;
+        TA.rkey = st_.rkey.ptr;
+        TA.run0 = dp ? st_.h_run[b] : 0;
+        TA.nrun = dp ? st_.h_run[b + 1] - st_.h_run[b] : 0;
+        TA.grad = st_.grad.ptr;
         const int64_t nchunks = ceil_div(TA.n, kChunk);
         switch (k / VW) {
         case 1: launch_tab_t<1>(TA, nchunks); break;
@@ -2217,7 +2421,7 @@ struct Trainer {
         // batches on one stream (the sort's blocks fill every SM, so
         // overlapping only delays the latency-bound batch kernels).
         const char* ov = getenv("MFM_B200_PLAN_OVERLAP");
-        const bool overlap = ov && *ov == '1';
+        const bool overlap = ov && *ov == '1' && !dp;
         const cudaStream_t hi = side_stream(device, 0);
         const cudaStream_t lo = overlap ? side_stream(device, 1) : hi;
         std::vector<std::pair<int64_t, int64_t>> win;
@@ -2246,21 +2450,27 @@ struct Trainer {
                     plan_tab_window(S[0], (int)e, win[w].first, win[w].second, lo);
                     MFM_CUDA(cudaEventRecord(ev.e[w], lo), "event");
                 }
+                if (dp) plan_tab_runs(S[0]);
                 for (size_t w = 0; w < win.size(); ++w) {
                     MFM_CUDA(cudaStreamWaitEvent(hi, ev.e[w], 0), "event");
                     for (int64_t b = win[w].first; b < win[w].second; ++b) {
                         const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                         const T inv_bsz = T(1) / (T)nrows;  // batch length (fm.rs:395-398)
+                        // data-parallel: this rank scores rows [rlo, rhi) of the batch
+                        const int64_t rlo = dp ? nrows * dp->rank / dp->world : 0;
+                        const int64_t rhi = dp ? nrows * (dp->rank + 1) / dp->world : nrows;
                         FwdArgs<T> A = base;
-                        A.pos0 = pos0;
-                        A.nrows = nrows;
+                        A.pos0 = pos0 + rlo;
+                        A.nrows = rhi - rlo;
+                        A.tab = base.tab + rlo * base.TW;
+                        A.grow = base.grow + rlo;
                         A.indptr = S[0].estart.ptr;  // rows by epoch position
                         A.indices = reinterpret_cast<const int32_t*>(S[0].pidx.ptr);
                         A.data = S[0].ex.ptr;
                         A.y = S[0].py.ptr;
                         A.sw = S[0].psw.ptr;
-                        launch_forward(A, nrows);
-                        launch_tab(b, inv_bsz, nrows);
+                        launch_forward(A, rhi - rlo);
+                        launch_tab(b, inv_bsz, nrows, rlo, rhi);
                     }
                 }
                 pt.mark("batches");
@@ -2573,12 +2783,13 @@ void fm_fit_device_impl(int device, cudaStream_t s, const int64_t* indptr,
                         const int32_t* indices, const T* data, int64_t n_rows, int64_t n_features,
                         const T* y, const T* sw, const int32_t* d_order, const mfm_train* c,
                         int64_t k, const mfm_dev_group* w0, const mfm_dev_group* w,
-                        const mfm_dev_group* v) {
+                        const mfm_dev_group* v, mfm_dp* dp = nullptr) {
     DeviceGuard guard(device);
     std::lock_guard<std::mutex> lk(device_mutex(device));
     Trainer<T> tr;
     tr.device = device;
     tr.s = s;
+    tr.dp = dp;
     PhaseTimer pt(s);
     tr.model = M_FM;
     tr.C = 1;
@@ -2598,8 +2809,48 @@ void fm_fit_device_impl(int device, cudaStream_t s, const int64_t* indptr,
     tr.device_group(1, w, n_features, 1, 0);
     tr.device_group(2, v, n_features * k, k, 1);
     FwdArgs<T> A = tr.prepare(c, data, y, nullptr, sw);
+    if (dp && !tr.S[0].tab)
+        fail(MFM_ERR_UNSUPPORTED,
+             fmt("data-parallel training supports k = %d, %d, %d or %d in this dtype, got %lld",
+                 16 / (int)sizeof(T), 32 / (int)sizeof(T), 64 / (int)sizeof(T),
+                 128 / (int)sizeof(T), (long long)k));
     pt.mark("setup");
     if (n_rows > 0) tr.run(A, pt);
+}
+
+void check_device_fit(const mfm_train* tr, int64_t k, int64_t n_rows, const mfm_dev_group* w0,
+                      const mfm_dev_group* w, const mfm_dev_group* v) {
+    if (!tr || tr->batch_size < 1) fail(MFM_ERR_INVALID, "batch_size must be >= 1");
+    if (tr->optimizer < MFM_OPT_SGD || tr->optimizer > MFM_OPT_FTRL)
+        fail(MFM_ERR_INVALID, fmt("unknown optimizer %d", tr->optimizer));
+    if (tr->loss != MFM_LOSS_LOGISTIC && tr->loss != MFM_LOSS_SQUARED)
+        fail(MFM_ERR_INVALID, fmt("unknown loss %d", tr->loss));
+    if (k < 1 || k > 1024)
+        fail(MFM_ERR_UNSUPPORTED,
+             fmt("CUDA training supports 1 <= k <= 1024, got %lld", (long long)k));
+    if (n_rows < 0 || n_rows >= ((int64_t)1 << 31))
+        fail(MFM_ERR_UNSUPPORTED, "n_rows must be in [0, 2^31)");
+    if (!w0 || !w || !v || !w0->param || !w->param || !v->param)
+        fail(MFM_ERR_INVALID, "parameter arrays must be provided");
+}
+
+void fit_device_dispatch(int dtype, int device, const int64_t* indptr, const int32_t* indices,
+                         const void* data, int64_t n_rows, int64_t n_features, const void* y,
+                         const void* sample_weight, const int32_t* row_orders,
+                         const mfm_train* tr, int64_t k, mfm_dev_group* w0, mfm_dev_group* w,
+                         mfm_dev_group* v, void* stream, mfm_dp* dp) {
+    check_device_fit(tr, k, n_rows, w0, w, v);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == MFM_DTYPE_F32)
+        fm_fit_device_impl<float>(device, s, indptr, indices, (const float*)data, n_rows,
+                                  n_features, (const float*)y, (const float*)sample_weight,
+                                  row_orders, tr, k, w0, w, v, dp);
+    else if (dtype == MFM_DTYPE_F64)
+        fm_fit_device_impl<double>(device, s, indptr, indices, (const double*)data, n_rows,
+                                   n_features, (const double*)y, (const double*)sample_weight,
+                                   row_orders, tr, k, w0, w, v, dp);
+    else
+        fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
 }
 }  // namespace mfm
 
@@ -2610,28 +2861,58 @@ extern "C" int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr,
                                  mfm_dev_group* w0, mfm_dev_group* w, mfm_dev_group* v,
                                  void* stream) {
     return guarded([&] {
-        if (!tr || tr->batch_size < 1) fail(MFM_ERR_INVALID, "batch_size must be >= 1");
-        if (tr->optimizer < MFM_OPT_SGD || tr->optimizer > MFM_OPT_FTRL)
-            fail(MFM_ERR_INVALID, fmt("unknown optimizer %d", tr->optimizer));
-        if (tr->loss != MFM_LOSS_LOGISTIC && tr->loss != MFM_LOSS_SQUARED)
-            fail(MFM_ERR_INVALID, fmt("unknown loss %d", tr->loss));
-        if (k < 1 || k > 1024)
-            fail(MFM_ERR_UNSUPPORTED,
-                 fmt("CUDA training supports 1 <= k <= 1024, got %lld", (long long)k));
-        if (n_rows < 0 || n_rows >= ((int64_t)1 << 31))
-            fail(MFM_ERR_UNSUPPORTED, "n_rows must be in [0, 2^31)");
-        if (!w0 || !w || !v || !w0->param || !w->param || !v->param)
-            fail(MFM_ERR_INVALID, "parameter arrays must be provided");
-        cudaStream_t s = (cudaStream_t)stream;
-        if (dtype == MFM_DTYPE_F32)
-            fm_fit_device_impl<float>(device, s, indptr, indices, (const float*)data, n_rows,
-                                      n_features, (const float*)y, (const float*)sample_weight,
-                                      row_orders, tr, k, w0, w, v);
-        else if (dtype == MFM_DTYPE_F64)
-            fm_fit_device_impl<double>(device, s, indptr, indices, (const double*)data, n_rows,
-                                       n_features, (const double*)y,
-                                       (const double*)sample_weight, row_orders, tr, k, w0, w, v);
-        else
-            fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
+        fit_device_dispatch(dtype, device, indptr, indices, data, n_rows, n_features, y,
+                            sample_weight, row_orders, tr, k, w0, w, v, stream, nullptr);
+    });
+}
+
+// ----------------------------------------------------- data-parallel group --
+
+extern "C" int mfm_dp_unique_id(unsigned char id[128]) {
+    return guarded([&] {
+        static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+        if (!id) fail(MFM_ERR_INVALID, "id must be provided");
+        ncclUniqueId u;
+        MFM_NCCL(nccl().GetUniqueId(&u), "ncclGetUniqueId");
+        memcpy(id, &u, sizeof(u));
+    });
+}
+
+extern "C" int mfm_dp_create(const unsigned char id[128], int world, int rank, int device,
+                             mfm_dp** out) {
+    return guarded([&] {
+        if (!id || !out) fail(MFM_ERR_INVALID, "id and out must be provided");
+        *out = nullptr;
+        if (world < 1 || rank < 0 || rank >= world)
+            fail(MFM_ERR_INVALID, fmt("rank %d outside [0, %d)", rank, world));
+        DeviceGuard guard(device);
+        ncclUniqueId u;
+        memcpy(&u, id, sizeof(u));
+        ncclComm_t c = nullptr;
+        MFM_NCCL(nccl().CommInitRank(&c, world, u, rank), "ncclCommInitRank");
+        *out = new mfm_dp{c, world, rank, device};
+    });
+}
+
+extern "C" int mfm_dp_destroy(mfm_dp* dp) {
+    return guarded([&] {
+        if (!dp) return;
+        DeviceGuard guard(dp->device);
+        const ncclComm_t c = dp->comm;
+        delete dp;
+        MFM_NCCL(nccl().CommDestroy(c), "ncclCommDestroy");
+    });
+}
+
+extern "C" int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr,
+                                    const int32_t* indices, const void* data, int64_t n_rows,
+                                    int64_t n_features, const void* y, const void* sample_weight,
+                                    const int32_t* row_orders, const mfm_train* tr, int64_t k,
+                                    mfm_dev_group* w0, mfm_dev_group* w, mfm_dev_group* v,
+                                    void* stream) {
+    return guarded([&] {
+        if (!dp) fail(MFM_ERR_INVALID, "a data-parallel group must be provided");
+        fit_device_dispatch(dtype, dp->device, indptr, indices, data, n_rows, n_features, y,
+                            sample_weight, row_orders, tr, k, w0, w, v, stream, dp);
     });
 }

@@ -1,0 +1,100 @@
+"""Synchronous data-parallel FM training over NCCL (one process per GPU).
+
+Every rank holds the whole training set, the parameters and the optimizer
+state. Each global mini-batch (the same row_orders chunking as one GPU) is cut
+into `world` contiguous row slices; rank r scores slice r, the per-key gradient
+sums over the batch's sorted union of touched keys are summed across ranks
+with one ncclAllReduce, and every rank applies the identical optimizer step:
+the mini-batch math of a one-GPU fit, up to summation order. The reference has
+no multi-GPU training; the single-GPU semantics it defines are
+rust/src/fm.rs:373-411 (batch loop) and rust/src/optimizer.rs:48-167 (steps).
+
+    import torch.distributed as dist
+    dist.init_process_group("gloo")            # any backend: it only carries the group id
+    group = DataParallelGroup(device=local_rank)
+    group.fm_fit_device(...)                    # every rank, same arguments
+    group.close()
+"""
+
+from __future__ import annotations
+
+import ctypes as ct
+
+from . import _lib
+
+ID_BYTES = 128
+
+
+def slice_rows(n_rows: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [lo, hi) of a batch of n_rows that rank `rank` of `world` scores
+    (the engine's split: floor(n*r/G), floor(n*(r+1)/G))."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside [0, {world})")
+    return n_rows * rank // world, n_rows * (rank + 1) // world
+
+
+def broadcast_unique_id(id_bytes: bytes | None, group=None) -> bytes:
+    """The NCCL group id made on rank 0, delivered to every rank through
+    torch.distributed (a 128-byte CPU tensor: works on gloo and on nccl)."""
+    import torch
+    import torch.distributed as dist
+
+    buf = torch.zeros(ID_BYTES, dtype=torch.uint8)
+    if dist.get_rank(group) == 0:
+        if id_bytes is None or len(id_bytes) != ID_BYTES:
+            raise ValueError("rank 0 must supply the 128-byte group id")
+        buf[:] = torch.frombuffer(bytearray(id_bytes), dtype=torch.uint8)
+    if dist.get_backend(group) == "nccl":
+        dev = torch.device("cuda", torch.cuda.current_device())
+        t = buf.to(dev)
+        dist.broadcast(t, src=0, group=group)
+        buf = t.cpu()
+    else:
+        dist.broadcast(buf, src=0, group=group)
+    return bytes(buf.numpy().tobytes())
+
+
+def new_unique_id() -> bytes:
+    out = ct.create_string_buffer(ID_BYTES)
+    if _lib.lib().mfm_dp_unique_id(out) != 0:
+        raise RuntimeError(_lib.last_error())
+    return out.raw
+
+
+class DataParallelGroup:
+    """One NCCL communicator over the torch.distributed world, bound to
+    `device` (default: LOCAL_RANK of the current process)."""
+
+    def __init__(self, device: int | None = None, group=None):
+        import os
+
+        import torch.distributed as dist
+
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = int(os.environ.get("LOCAL_RANK", "0")) if device is None else int(device)
+        uid = broadcast_unique_id(new_unique_id() if self.rank == 0 else None, group)
+        h = ct.c_void_p()
+        if _lib.lib().mfm_dp_create(uid, self.world, self.rank, self.device, ct.byref(h)) != 0:
+            raise RuntimeError(_lib.last_error())
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def fm_fit_device(self, dtype, indptr, indices, data, n_rows, n_features, y, sample_weight,
+                      row_orders, train, k, w0, w, v, stream):
+        """mfm_fm_fit_device_dp: device pointers (ints) in the compute dtype,
+        `train` an _lib.Train, w0/w/v _lib.DevGroup; raises RuntimeError with
+        the engine's message on failure."""
+        rc = _lib.lib().mfm_fm_fit_device_dp(self._h, dtype, indptr, indices, data, n_rows,
+                                             n_features, y, sample_weight, row_orders, train, k,
+                                             w0, w, v, stream)
+        if rc != 0:
+            raise RuntimeError(_lib.last_error())
+
+    def close(self):
+        if self._h:
+            _lib.lib().mfm_dp_destroy(self._h)
+            self._h = None

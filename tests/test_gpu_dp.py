@@ -1,0 +1,103 @@
+"""Data-parallel FM training on 2 GPUs (NCCL): every rank ends bitwise equal
+to the others, and equal to a one-GPU fit of the same inputs within the
+float64 training tolerance (1e-7 relative / 1e-9 absolute: only the summation
+order differs — per-rank partial sums, then the cross-rank sum)."""
+
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+from modern_fm_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+K, BATCH, EPOCHS = 8, 512, 2
+
+
+def _data():
+    X, _ = workloads.ctr_fm(n_rows=6000, seed=21, space=2**14, vocab=2**11)
+    rng = np.random.default_rng(3)
+    y = (rng.random(X.n_rows) < 0.3).astype(np.float64)
+    sw = rng.uniform(0.5, 1.5, X.n_rows)
+    V = rng.normal(0, 0.05, (X.n_features, K))
+    ro = workloads.row_orders(X.n_rows, EPOCHS, seed=5).astype(np.int32)
+    return X, y, sw, V, ro
+
+
+def _fit(opt, device, group=None):
+    import torch
+
+    from modern_fm_b200 import _lib
+
+    X, y, sw, V0, ro = _data()
+    dev = torch.device("cuda", device)
+    t = lambda a, dt=torch.float64: torch.as_tensor(np.ascontiguousarray(a), dtype=dt,  # noqa
+                                                    device=dev)
+    ip, ix, dv = t(X.indptr, torch.int64), t(X.indices, torch.int32), t(X.data)
+    yy, ss, rot = t(y), t(sw), t(ro, torch.int32)
+    w0, w, V = t([0.0]), t(np.zeros(X.n_features)), t(V0)
+    state = [t(np.zeros(1)), t(np.zeros(X.n_features)), t(np.zeros_like(V0))]
+    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS[opt], 0.05, 0.0, 1e-5, 0.0, 1e-5,
+                    0.9, 0.999, 1e-8, 1.0, 0.0, None, EPOCHS, BATCH)
+    g = [_lib.DevGroup(p.data_ptr(), a.data_ptr() if opt == "adagrad" else None, None, None,
+                       None, None, None) for p, a in zip((w0, w, V), state)]
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    args = (_lib.MFM_DTYPE_F64, ip.data_ptr(), ix.data_ptr(), dv.data_ptr(), X.n_rows,
+            X.n_features, yy.data_ptr(), ss.data_ptr(), rot.data_ptr(), tr, K, g[0], g[1], g[2],
+            stream)
+    if group is None:
+        rc = _lib.lib().mfm_fm_fit_device(args[0], device, *args[1:])
+        assert rc == 0, _lib.last_error()
+    else:
+        group.fm_fit_device(*args)
+    torch.cuda.synchronize(dev)
+    return {n: a.cpu().numpy() for n, a in (("w0", w0), ("w", w), ("V", V),
+                                            ("acc_w", state[1]), ("acc_V", state[2]))}
+
+
+def _worker(rank, world, port, opt, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from modern_fm_b200 import dp
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    group = None
+    try:
+        group = dp.DataParallelGroup(device=rank)
+        res = _fit(opt, rank, group)
+        np.savez(os.path.join(out_dir, f"r{rank}.npz"), **res)
+    finally:
+        if group is not None:
+            group.close()
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("opt", ["adagrad", "adam"])
+def test_two_gpu_data_parallel_fit(opt):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_worker, args=(2, _free_port(), opt, d), nprocs=2, join=True)
+        ranks = [dict(np.load(os.path.join(d, f"r{r}.npz"))) for r in range(2)]
+    for key in ranks[0]:
+        np.testing.assert_array_equal(ranks[0][key], ranks[1][key], err_msg=key)
+    one = _fit(opt, 0)
+    keys = ("w0", "w", "V", "acc_w", "acc_V") if opt == "adagrad" else ("w0", "w", "V")
+    for key in keys:
+        np.testing.assert_allclose(ranks[0][key], one[key], rtol=1e-7, atol=1e-9, err_msg=key)
+    assert np.abs(ranks[0]["V"] - _data()[3]).max() > 1e-4  # training moved the factors
