@@ -200,24 +200,22 @@ TRAIN_ROWS = 10_000_000
 TRAIN_BATCH = 4096
 
 
-def train_measure(args, rank, world, local, dev_t, L, _lib):
-    """FM AdaGrad training on the large CTR config: 10M rows, batch 4096,
-    k=16, float32, one epoch per step. Returns the `train` object of the
-    JSON line (rank 0) or None."""
+def train_inputs(n, seed, dev_t, L, _lib):
+    """The training workload on the device: CTR-shaped CSR, labels drawn from a
+    planted FM with N(0, 0.1) parameters at ~3 % positives, unit sample
+    weights, one shuffled row order."""
     import torch
 
     from modern_fm_b200 import workloads as WL
 
-    n = args.train_rows
-    X = WL.ctr_fm_torch(n, SEED + 100 + rank, device=dev_t)
+    X = WL.ctr_fm_torch(n, seed, device=dev_t)
     g = torch.Generator(device=dev_t)
-    g.manual_seed(4321 + rank)
-    # labels from a planted FM with N(0, 0.1) parameters at ~3 % positives
+    g.manual_seed(seed + 4219)
     wp = (torch.randn(N_FEATURES, generator=g, device=dev_t) * 0.1).contiguous()
     Vp = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.1).contiguous()
     sc = torch.empty(n, dtype=torch.float32, device=dev_t)
     stream = torch.cuda.current_stream(dev_t)
-    rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32, local, X["indptr"].data_ptr(),
+    rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32, dev_t.index, X["indptr"].data_ptr(),
                                  X["indices"].data_ptr(), X["data"].data_ptr(), n, 0.0,
                                  wp.data_ptr(), Vp.data_ptr(), K, sc.data_ptr(), stream.cuda_stream)
     if rc:
@@ -232,6 +230,19 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     y = (torch.rand(n, generator=g, device=dev_t) < torch.sigmoid(sc + 0.5 * (lo + hi))).float()
     sw = torch.ones(n, device=dev_t)
     order = torch.randperm(n, generator=g, device=dev_t).to(torch.int32).contiguous()
+    V0 = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.01).contiguous()
+    return X, y, sw, order, V0
+
+
+def train_measure(args, rank, world, local, dev_t, L, _lib):
+    """FM AdaGrad training on the large CTR config: 10M rows, batch 4096,
+    k=16, float32, one epoch per step. Returns the `train` object of the
+    JSON line (rank 0) or None."""
+    import torch
+
+    n = args.train_rows
+    X, y, sw, order, V0 = train_inputs(n, SEED + 100 + rank, dev_t, L, _lib)
+    stream = torch.cuda.current_stream(dev_t)
     # algorithmic bytes of one epoch: per row the scoring gathers (2976 B) + y,
     # sample weight; per (batch, touched feature) param and AdaGrad state read
     # and written: 4 x (k+1) x 4 B
@@ -246,7 +257,7 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
 
     w0 = torch.zeros(1, device=dev_t)
     w = torch.zeros(N_FEATURES, device=dev_t)
-    V = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.01).contiguous()
+    V = V0
     acc0, accw, accV = torch.zeros(1, device=dev_t), torch.zeros_like(w), torch.zeros_like(V)
     tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
                     1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, None, 1, TRAIN_BATCH)
@@ -349,6 +360,51 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     return out
 
 
+def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
+    """One data-parallel fit across all ranks (N > 1): the same 10M-row epoch,
+    every global batch of 4096 rows split over the ranks, one allreduce of the
+    batch's per-key gradient sums per batch. Strong scaling of one fit."""
+    import torch
+
+    from modern_fm_b200 import dp as DP
+
+    n = args.train_rows
+    X, y, sw, order, V = train_inputs(n, SEED + 100, dev_t, L, _lib)  # same data on every rank
+    stream = torch.cuda.current_stream(dev_t)
+    w0, w = torch.zeros(1, device=dev_t), torch.zeros(N_FEATURES, device=dev_t)
+    acc0, accw, accV = torch.zeros(1, device=dev_t), torch.zeros_like(w), torch.zeros_like(V)
+    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
+                    1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, None, 1, TRAIN_BATCH)
+    grp = [_lib.DevGroup(p.data_ptr(), a.data_ptr(), None, None, None, None, None)
+           for p, a in ((w0, acc0), (w, accw), (V, accV))]
+    group = DP.DataParallelGroup(device=local)
+    try:
+        def epoch():
+            group.fm_fit_device(_lib.MFM_DTYPE_F32, X["indptr"].data_ptr(),
+                                X["indices"].data_ptr(), X["data"].data_ptr(), n, N_FEATURES,
+                                y.data_ptr(), sw.data_ptr(), order.data_ptr(), tr, K, grp[0],
+                                grp[1], grp[2], stream.cuda_stream)
+
+        epoch()
+        torch.cuda.synchronize()
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.train_steps):
+            epoch()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(t0.elapsed_time(t1) / args.train_steps, world)
+    finally:
+        group.close()
+    if rank != 0:
+        return None
+    return {"metric": "FM AdaGrad data-parallel training rows/s (one fit, global batch 4096 "
+                      "split over the ranks, NCCL allreduce per batch)",
+            "value": n / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "rows": n,
+            "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong"}
+
+
 def run_ours(args):
     import torch
 
@@ -363,8 +419,11 @@ def run_ours(args):
     L = _lib.lib()
     if args.train_only:
         train = train_measure(args, rank, world, local, dev_t, L, _lib)
+        train_dp = train_dp_measure(args, rank, world, local, dev_t, L, _lib) if world > 1 else None
         if train:
             train["n_gpus"] = world
+            if train_dp:
+                train["train_dp"] = train_dp
             print(json.dumps(train), flush=True)
         if world > 1:
             import torch.distributed as dist
@@ -460,6 +519,8 @@ def run_ours(args):
                          "single-threaded, rust/src/fm.rs:58-70)"}
 
     train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
+    train_dp = (train_dp_measure(args, rank, world, local, dev_t, L, _lib)
+                if world > 1 and not args.no_train else None)
 
     if rank == 0:
         rows_total = N_ROWS * world
@@ -487,6 +548,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if train:
             line["train"] = train
+        if train_dp:
+            line["train_dp"] = train_dp
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
