@@ -61,11 +61,15 @@ __global__ void __launch_bounds__(256)
 }
 
 // Value writers of the scatter: plain (the value itself) or, on the last
-// pass, two arrays gathered at segment start + value.
+// pass, two arrays gathered at segment start + value. `load` is issued for all
+// of a thread's values before any `store`, so the gathers overlap.
 struct PlainValue {
-    __device__ __forceinline__ void operator()(uint32_t* vout, int64_t dst, int64_t,
-                                               uint32_t val) const {
-        vout[dst] = val;
+    struct P {
+        uint32_t v;
+    };
+    __device__ __forceinline__ P load(int64_t, uint32_t val) const { return P{val}; }
+    __device__ __forceinline__ void store(uint32_t* vout, int64_t dst, const P& p) const {
+        vout[dst] = p.v;
     }
 };
 template <class T>
@@ -73,10 +77,16 @@ struct RecGather {
     const uint32_t* a;  // -> vout
     const T* b;         // -> bout
     T* bout;
-    __device__ __forceinline__ void operator()(uint32_t* vout, int64_t dst, int64_t seg0,
-                                               uint32_t val) const {
-        vout[dst] = a[seg0 + val];
-        bout[dst] = b[seg0 + val];
+    struct P {
+        uint32_t v;
+        T x;
+    };
+    __device__ __forceinline__ P load(int64_t seg0, uint32_t val) const {
+        return P{__ldg(a + seg0 + val), __ldg(b + seg0 + val)};
+    }
+    __device__ __forceinline__ void store(uint32_t* vout, int64_t dst, const P& p) const {
+        vout[dst] = p.v;
+        bout[dst] = p.x;
     }
 };
 
@@ -154,11 +164,21 @@ __global__ void __launch_bounds__(kSortNT)
             sval[lp] = val[i];
         }
     __syncthreads();
-    for (int j = t; j < n; j += kSortNT) {
-        const uint32_t k = skey[j];
-        const int64_t dst = seg0 + (int64_t)(base[(k >> shift) & 255u] + (uint32_t)j);
-        kout[dst] = k;
-        out(vout, dst, seg0, sval[j]);
+    typename Out::P pay[kSortItems];
+#pragma unroll
+    for (int u = 0; u < kSortItems; ++u) {
+        const int j = t + u * kSortNT;
+        if (j < n) pay[u] = out.load(seg0, sval[j]);
+    }
+#pragma unroll
+    for (int u = 0; u < kSortItems; ++u) {
+        const int j = t + u * kSortNT;
+        if (j < n) {
+            const uint32_t k = skey[j];
+            const int64_t dst = seg0 + (int64_t)(base[(k >> shift) & 255u] + (uint32_t)j);
+            kout[dst] = k;
+            out.store(vout, dst, pay[u]);
+        }
     }
 }
 
