@@ -793,6 +793,10 @@ __global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
 // Stream 1 (FEAT) payload: [g_c x_a] (w gradient);
 // stream 2 (SLOT) payload per ordered pair (a, b != a), slot (i_a, f_b):
 // [g_c x_a x_b V[i_b, f_a, c, :]] (FfmGradAccum::add_row, rust/src/ffm.rs:129-171).
+// Rows of up to kFfmStage nonzeros are staged per warp in shared memory
+// (index, value, field): pair decoding then needs no dependent global loads.
+constexpr int kFfmStage = 64;
+
 template <class T, int VEC>
 __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
     extern __shared__ unsigned char smraw[];
@@ -800,6 +804,11 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     T* logit = reinterpret_cast<T*>(smraw) + (size_t)wib * 2 * C;
     T* gs = logit + C;
+    T* s_x = reinterpret_cast<T*>(smraw) + (size_t)8 * 2 * C + (size_t)wib * kFfmStage;
+    int32_t* s_ix = reinterpret_cast<int32_t*>(reinterpret_cast<T*>(smraw) + (size_t)8 * 2 * C +
+                                               (size_t)8 * kFfmStage) +
+                    (size_t)wib * 2 * kFfmStage;
+    int32_t* s_f = s_ix + kFfmStage;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
          j += nwarps) {
@@ -807,25 +816,66 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
         const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
         const int32_t* ix = A.indices + rb;
         const T* dv = A.data + rb;
+        const bool staged = z <= kFfmStage;
+        if (staged) {
+            for (int q = lane; q < z; q += 32) {
+                const int32_t i = ix[q];
+                s_ix[q] = i;
+                s_x[q] = dv[q];
+                s_f[q] = A.fid[i];
+            }
+            __syncwarp();
+        }
         for (int c = 0; c < C; ++c) {  // ffm_score_row, rust/src/ffm.rs:18-45
             T acc = T(0);
-            for (int64_t q = lane; q < z; q += 32) acc += A.w[(int64_t)ix[q] * C + c] * dv[q];
-            int64_t a = 0, b = 1 + lane;
-            pair_step(a, b, z);
-            while (a < z - 1) {
-                const int32_t ia = ix[a], ib = ix[b];
-                const int fa = A.fid[ia], fb = A.fid[ib];
-                const T* pa = A.v + (((int64_t)ia * F + fb) * C + c) * k;
-                const T* pb = A.v + (((int64_t)ib * F + fa) * C + c) * k;
-                T dot = T(0);
-                for (int t = 0; t < k; t += VEC) {
-                    const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
-#pragma unroll
-                    for (int u = 0; u < VEC; ++u) dot += qa.v[u] * qb.v[u];
-                }
-                acc += dot * dv[a] * dv[b];
-                b += 32;
+            if (staged) {
+                for (int q = lane; q < z; q += 32) acc += A.w[(int64_t)s_ix[q] * C + c] * s_x[q];
+                int64_t a = 0, b = 1 + lane;
                 pair_step(a, b, z);
+                while (a < z - 1) {  // two pairs per step, all four latent rows in flight
+                    int64_t a2 = a, b2 = b + 32;
+                    pair_step(a2, b2, z);
+                    const bool two = a2 < z - 1;
+                    const T* pa = A.v + (((int64_t)s_ix[a] * F + s_f[b]) * C + c) * k;
+                    const T* pb = A.v + (((int64_t)s_ix[b] * F + s_f[a]) * C + c) * k;
+                    const T* pc = two ? A.v + (((int64_t)s_ix[a2] * F + s_f[b2]) * C + c) * k : pa;
+                    const T* pd = two ? A.v + (((int64_t)s_ix[b2] * F + s_f[a2]) * C + c) * k : pb;
+                    T d1 = T(0), d2 = T(0);
+                    for (int t = 0; t < k; t += VEC) {
+                        const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
+                        const Vec<T, VEC> qc = ldg_vec<T, VEC>(pc + t), qd = ldg_vec<T, VEC>(pd + t);
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) {
+                            d1 += qa.v[u] * qb.v[u];
+                            d2 += qc.v[u] * qd.v[u];
+                        }
+                    }
+                    acc += d1 * s_x[a] * s_x[b];
+                    if (!two) break;
+                    acc += d2 * s_x[a2] * s_x[b2];
+                    a = a2;
+                    b = b2 + 32;
+                    pair_step(a, b, z);
+                }
+            } else {
+                for (int64_t q = lane; q < z; q += 32) acc += A.w[(int64_t)ix[q] * C + c] * dv[q];
+                int64_t a = 0, b = 1 + lane;
+                pair_step(a, b, z);
+                while (a < z - 1) {
+                    const int32_t ia = ix[a], ib = ix[b];
+                    const int fa = A.fid[ia], fb = A.fid[ib];
+                    const T* pa = A.v + (((int64_t)ia * F + fb) * C + c) * k;
+                    const T* pb = A.v + (((int64_t)ib * F + fa) * C + c) * k;
+                    T dot = T(0);
+                    for (int t = 0; t < k; t += VEC) {
+                        const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) dot += qa.v[u] * qb.v[u];
+                    }
+                    acc += dot * dv[a] * dv[b];
+                    b += 32;
+                    pair_step(a, b, z);
+                }
             }
             acc = warp_sum(acc);
             if (lane == 0) logit[c] = A.w0[c] + acc;
@@ -841,16 +891,33 @@ __global__ void __launch_bounds__(256) ffm_forward_kernel(FwdArgs<T> A) {
             A.pay1[(int64_t)A.inv1[A.seg1 + e1 + a] * A.W1 + c] = gs[c] * dv[a];
         }
         const int64_t e2 = A.estart2[pos] - A.seg2;
-        const int64_t tot = z * (z - 1) * CK;
-        for (int64_t q = lane; q < tot; q += 32) {
-            const int64_t pe = q / CK;
-            const int col = (int)(q - pe * CK);
-            const int64_t a = pe / (z - 1), bi = pe - a * (z - 1), b = bi < a ? bi : bi + 1;
-            const int c = col / k, t = col - c * k;
-            const int32_t ib = ix[b];
-            const int fa = A.fid[ix[a]];
-            A.pay2[(int64_t)A.inv2[A.seg2 + e2 + pe] * A.W2 + col] =
-                gs[c] * dv[a] * dv[b] * A.v[(((int64_t)ib * F + fa) * C + c) * k + t];
+        if (staged) {  // one ordered pair per lane step: k-wide vector gathers and stores
+            for (int64_t pe = lane; pe < z * (z - 1); pe += 32) {
+                const int64_t a = pe / (z - 1), bi = pe - a * (z - 1), b = bi < a ? bi : bi + 1;
+                const T xa = s_x[a], xb = s_x[b];
+                const T* src = A.v + ((int64_t)s_ix[b] * F + s_f[a]) * CK;
+                T* P = A.pay2 + (int64_t)A.inv2[A.seg2 + e2 + pe] * A.W2;
+                for (int c = 0; c < C; ++c)
+                    for (int t = 0; t < k; t += VEC) {
+                        const Vec<T, VEC> q = ldg_vec<T, VEC>(src + c * k + t);
+                        Vec<T, VEC> o;
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) o.v[u] = gs[c] * xa * xb * q.v[u];
+                        *reinterpret_cast<Vec<T, VEC>*>(P + c * k + t) = o;
+                    }
+            }
+        } else {
+            const int64_t tot = z * (z - 1) * CK;
+            for (int64_t q = lane; q < tot; q += 32) {
+                const int64_t pe = q / CK;
+                const int col = (int)(q - pe * CK);
+                const int64_t a = pe / (z - 1), bi = pe - a * (z - 1), b = bi < a ? bi : bi + 1;
+                const int c = col / k, t = col - c * k;
+                const int32_t ib = ix[b];
+                const int fa = A.fid[ix[a]];
+                A.pay2[(int64_t)A.inv2[A.seg2 + e2 + pe] * A.W2 + col] =
+                    gs[c] * dv[a] * dv[b] * A.v[(((int64_t)ib * F + fa) * C + c) * k + t];
+            }
         }
         __syncwarp();
     }
@@ -2236,12 +2303,14 @@ struct Trainer {
         constexpr int maxv = 16 / sizeof(T);
         const bool v4 = k % maxv == 0, v2 = k % 2 == 0;
         if (model == M_FFM) {
+            // + per warp: staged values, indices and fields of a row
+            const size_t smf = sm + (size_t)8 * kFfmStage * (sizeof(T) + 2 * sizeof(int32_t));
             if (v4)
-                ffm_forward_kernel<T, maxv><<<grid, 256, sm, s>>>(A);
+                ffm_forward_kernel<T, maxv><<<grid, 256, smf, s>>>(A);
             else if (v2)
-                ffm_forward_kernel<T, 2><<<grid, 256, sm, s>>>(A);
+                ffm_forward_kernel<T, 2><<<grid, 256, smf, s>>>(A);
             else
-                ffm_forward_kernel<T, 1><<<grid, 256, sm, s>>>(A);
+                ffm_forward_kernel<T, 1><<<grid, 256, smf, s>>>(A);
         } else {
             if (v4)
                 fwfm_forward_kernel<T, maxv><<<grid, 256, sm, s>>>(A);
