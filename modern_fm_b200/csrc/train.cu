@@ -540,6 +540,7 @@ __device__ __forceinline__ void fm_forward_dev(const FwdArgs<T>& A, int lgc, uns
                 my_i = A.indices[rb + base + lane];
                 my_x = A.data[rb + base + lane];
             }
+#pragma unroll 4  // four nonzeros' gathers in flight
             for (int t = 0; t < nh; t += G) {
                 const int src = t + grp;
                 const int32_t i = __shfl_sync(0xffffffffu, my_i, src);
@@ -595,6 +596,7 @@ __device__ __forceinline__ void fm_forward_dev(const FwdArgs<T>& A, int lgc, uns
                 my_i = A.indices[rb + base + lane];
                 my_x = A.data[rb + base + lane];
             }
+#pragma unroll 4  // four nonzeros' gathers in flight
             for (int t = 0; t < nh; t += G) {
                 const int src = t + grp;
                 const int32_t i = __shfl_sync(0xffffffffu, my_i, src);
