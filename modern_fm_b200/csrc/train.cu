@@ -770,6 +770,16 @@ struct Trainer {
         TA.run0 = dp ? st_.h_run[b] : 0;
         TA.nrun = dp ? st_.h_run[b + 1] - st_.h_run[b] : 0;
         TA.grad = st_.grad.ptr;
+        for (auto& r : TA.pre) r = L2Range{nullptr, 0};
+        if (b + 1 < nb) {  // the next batch's epoch-order rows, pulled into L2 by stage 2
+            const int64_t p1 = (b + 1) * B, n1 = std::min(B, n_rows - p1);
+            const int64_t e0 = st_.h_seg[b + 1], ne = st_.h_seg[b + 2] - e0;
+            TA.pre[0] = L2Range{st_.pidx.ptr + e0, ne * (int64_t)sizeof(uint32_t)};
+            TA.pre[1] = L2Range{st_.ex.ptr + e0, ne * (int64_t)sizeof(T)};
+            TA.pre[2] = L2Range{st_.estart.ptr + p1, (n1 + 1) * (int64_t)sizeof(int64_t)};
+            TA.pre[3] = L2Range{st_.py.ptr + p1, n1 * (int64_t)sizeof(T)};
+            TA.pre[4] = L2Range{st_.psw.ptr + p1, n1 * (int64_t)sizeof(T)};
+        }
         const int64_t nchunks = ceil_div(TA.n, kChunk);
         switch (k / VW) {
         case 1: launch_tab_t<1>(TA, nchunks); break;
@@ -922,6 +932,12 @@ struct Trainer {
                         A.data = S[0].ex.ptr;
                         A.y = S[0].py.ptr;
                         A.sw = S[0].psw.ptr;
+                        {  // stage 1's sorted stream of this batch, pulled into L2 by the forward
+                            const int64_t sg = S[0].h_seg[b], ne = S[0].h_seg[b + 1] - sg;
+                            A.pre[0] = L2Range{S[0].keys + sg, ne * (int64_t)sizeof(uint32_t)};
+                            A.pre[1] = L2Range{S[0].rrow + sg, ne * (int64_t)sizeof(uint32_t)};
+                            A.pre[2] = L2Range{S[0].rx.ptr + sg, ne * (int64_t)sizeof(T)};
+                        }
                         launch_forward(A, rhi - rlo);
                         launch_tab(b, inv_bsz, nrows, rlo, rhi);
                     }

@@ -34,6 +34,7 @@ struct FwdArgs {
     T* pay2;
     int W2;
     T* grow;  // (nrows, C) per-row loss gradients, summed into the w0 gradient
+    L2Range pre[3];  // row-table path: stage 1's sorted (key, row, x) of this batch
     T* tab;   // row table (nrows, TW): [S (k) | g | pad] (binary FM row-table path)
     int TW;
 };
@@ -263,7 +264,11 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
     using Sh = RowsShape<T, VEC, L, LR, CAP>;
     const int lane = threadIdx.x & 31, rl = lane & (LR - 1), grp = rl / L, l = rl % L;
     const bool act = l < A.k / VEC;
-    if (TAB) pdl_trigger();
+    if (TAB) {
+        pdl_trigger();
+        if (threadIdx.x == 0)
+            for (int r = 0; r < 3; ++r) prefetch_slice(A.pre[r], blockIdx.x, gridDim.x);
+    }
     for (int64_t j = slot0;; j += nslots) {
         const bool live = j < A.nrows;
         if (!__any_sync(0xffffffffu, live)) break;

@@ -35,6 +35,27 @@ struct OptDev {
 // Every thread of a PDL kernel calls pdl_wait before its first write and
 // before it exits, so this grid's completion implies its predecessor's.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// A contiguous byte range to pull into L2 ahead of the kernel that reads it.
+struct L2Range {
+    const void* p;
+    int64_t bytes;
+};
+// Slice `part` of `nparts` of r, trimmed to 16-byte boundaries, requested with
+// one bulk L2 prefetch (no registers, no wait; a hint the hardware may drop).
+__device__ __forceinline__ void prefetch_slice(const L2Range& r, int64_t part, int64_t nparts) {
+    if (!r.p || r.bytes <= 0) return;
+    const int64_t per = (r.bytes + nparts - 1) / nparts;
+    const uintptr_t base = (uintptr_t)r.p;
+    uintptr_t lo = base + (uintptr_t)(per * part), hi = lo + (uintptr_t)per;
+    const uintptr_t end = base + (uintptr_t)r.bytes;
+    if (hi > end) hi = end;
+    lo = (lo + 15) & ~(uintptr_t)15;
+    hi &= ~(uintptr_t)15;
+    if (hi <= lo) return;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"((uint32_t)(hi - lo))
+                 : "memory");
+}
+
 __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }

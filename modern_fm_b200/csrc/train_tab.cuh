@@ -54,6 +54,7 @@ struct TabArgs {
     const uint32_t* rkey;  // key of each run of the epoch
     int64_t run0, nrun;    // this batch's runs: [run0, run0 + nrun)
     T* grad;
+    L2Range pre[5];        // the next batch's epoch-order rows, for its forward
 };
 
 // float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
@@ -198,6 +199,8 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
     constexpr int K = VEC * NV;
     const unsigned FULL = 0xffffffffu;
     pdl_trigger();
+    if (threadIdx.x == 0)
+        for (int r = 0; r < 5; ++r) prefetch_slice(A.pre[r], blockIdx.x, gridDim.x);
     if (blockIdx.x == gridDim.x - 1) {
         __shared__ T sm[256];
         pdl_wait();
