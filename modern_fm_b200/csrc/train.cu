@@ -696,12 +696,13 @@ struct Trainer {
             else
                 ffm_forward_kernel<T, 1><<<grid, 256, smf, s>>>(A);
         } else {
+            const size_t smf = sm + (size_t)8 * kFfmStage * (sizeof(T) + 2 * sizeof(int32_t));
             if (v4)
-                fwfm_forward_kernel<T, maxv><<<grid, 256, sm, s>>>(A);
+                fwfm_forward_kernel<T, maxv><<<grid, 256, smf, s>>>(A);
             else if (v2)
-                fwfm_forward_kernel<T, 2><<<grid, 256, sm, s>>>(A);
+                fwfm_forward_kernel<T, 2><<<grid, 256, smf, s>>>(A);
             else
-                fwfm_forward_kernel<T, 1><<<grid, 256, sm, s>>>(A);
+                fwfm_forward_kernel<T, 1><<<grid, 256, smf, s>>>(A);
         }
         MFM_CHECK_LAUNCH("forward");
     }

@@ -498,6 +498,12 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     T* logit = reinterpret_cast<T*>(smraw) + (size_t)wib * 2 * C;
     T* gs = logit + C;
+    // rows of up to kFfmStage nonzeros: index, value and field staged per warp
+    T* s_x = reinterpret_cast<T*>(smraw) + (size_t)8 * 2 * C + (size_t)wib * kFfmStage;
+    int32_t* s_ix = reinterpret_cast<int32_t*>(reinterpret_cast<T*>(smraw) + (size_t)8 * 2 * C +
+                                               (size_t)8 * kFfmStage) +
+                    (size_t)wib * 2 * kFfmStage;
+    int32_t* s_f = s_ix + kFfmStage;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < A.nrows;
          j += nwarps) {
@@ -505,14 +511,25 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
         const int64_t rb = A.indptr[row], z = A.indptr[row + 1] - rb;
         const int32_t* ix = A.indices + rb;
         const T* dv = A.data + rb;
+        const bool staged = z <= kFfmStage;
+        if (staged) {
+            for (int q = lane; q < z; q += 32) {
+                const int32_t i = ix[q];
+                s_ix[q] = i;
+                s_x[q] = dv[q];
+                s_f[q] = A.fid[i];
+            }
+            __syncwarp();
+        }
         for (int c = 0; c < C; ++c) {  // fwfm_score_row, rust/src/fwfm.rs:24-53
             T acc = T(0);
-            for (int64_t q = lane; q < z; q += 32) acc += A.w[(int64_t)ix[q] * C + c] * dv[q];
+            for (int64_t q = lane; q < z; q += 32)
+                acc += A.w[(int64_t)(staged ? s_ix[q] : ix[q]) * C + c] * (staged ? s_x[q] : dv[q]);
             int64_t a = 0, b = 1 + lane;
             pair_step(a, b, z);
             while (a < z - 1) {
-                const int32_t ia = ix[a], ib = ix[b];
-                const int fa = A.fid[ia], fb = A.fid[ib];
+                const int32_t ia = staged ? s_ix[a] : ix[a], ib = staged ? s_ix[b] : ix[b];
+                const int fa = staged ? s_f[a] : A.fid[ia], fb = staged ? s_f[b] : A.fid[ib];
                 const T rw = A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
                 const T* pa = A.v + ((int64_t)ia * C + c) * k;
                 const T* pb = A.v + ((int64_t)ib * C + c) * k;
@@ -535,38 +552,72 @@ __global__ void __launch_bounds__(256) fwfm_forward_kernel(FwdArgs<T> A) {
         for (int c = lane; c < C; c += 32) A.grow[j * C + c] = gs[c];
         const int64_t e1 = A.estart1[pos] - A.seg1;
         const int W1u = CK + C;  // used columns: [v (C*k) | w (C)]
-        for (int64_t q = lane; q < z * W1u; q += 32) {
-            const int64_t a = q / W1u;
-            const int col = (int)(q - a * W1u);
-            T val;
-            if (col >= CK) {
-                val = gs[col - CK] * dv[a];
-            } else {
-                const int c = col / k, t = col - c * k;
-                const int fa = A.fid[ix[a]];
-                T s = T(0);
-                for (int64_t b = 0; b < z; ++b) {
-                    if (b == a) continue;
-                    const int32_t ib = ix[b];
-                    const int fb = A.fid[ib];
-                    const T rw = A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
-                    s += rw * dv[b] * A.v[((int64_t)ib * C + c) * k + t];
+        if (staged) {  // lane per entry a: sum over partners b with k-wide vectors
+            for (int a = lane; a < z; a += 32) {
+                const T xa = s_x[a];
+                const int fa = s_f[a];
+                T* P = A.pay1 + (int64_t)A.inv1[A.seg1 + e1 + a] * W1;
+                for (int c = 0; c < C; ++c) {
+                    for (int t = 0; t < k; t += VEC) {
+                        T sum[VEC];
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) sum[u] = T(0);
+                        for (int b = 0; b < z; ++b) {
+                            if (b == a) continue;
+                            const int fb = s_f[b];
+                            const T rw =
+                                A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
+                            const Vec<T, VEC> q =
+                                ldg_vec<T, VEC>(A.v + ((int64_t)s_ix[b] * C + c) * k + t);
+#pragma unroll
+                            for (int u = 0; u < VEC; ++u) sum[u] += rw * s_x[b] * q.v[u];
+                        }
+                        Vec<T, VEC> o;
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u) o.v[u] = gs[c] * xa * sum[u];
+                        *reinterpret_cast<Vec<T, VEC>*>(P + c * k + t) = o;
+                    }
+                    P[CK + c] = gs[c] * xa;
                 }
-                val = gs[c] * dv[a] * s;
             }
-            A.pay1[(int64_t)A.inv1[A.seg1 + e1 + a] * W1 + col] = val;
+        } else {
+            for (int64_t q = lane; q < z * W1u; q += 32) {
+                const int64_t a = q / W1u;
+                const int col = (int)(q - a * W1u);
+                T val;
+                if (col >= CK) {
+                    val = gs[col - CK] * dv[a];
+                } else {
+                    const int c = col / k, t = col - c * k;
+                    const int fa = A.fid[ix[a]];
+                    T s = T(0);
+                    for (int64_t b = 0; b < z; ++b) {
+                        if (b == a) continue;
+                        const int32_t ib = ix[b];
+                        const int fb = A.fid[ib];
+                        const T rw = A.r[(int64_t)(fa <= fb ? fa * F + fb : fb * F + fa) * C + c];
+                        s += rw * dv[b] * A.v[((int64_t)ib * C + c) * k + t];
+                    }
+                    val = gs[c] * dv[a] * s;
+                }
+                A.pay1[(int64_t)A.inv1[A.seg1 + e1 + a] * W1 + col] = val;
+            }
         }
         const int64_t e2 = A.estart2[pos] - A.seg2;
         int64_t a = 0, b = 1 + lane, pi = lane;
         pair_step(a, b, z);
         while (a < z - 1) {
-            const int32_t ia = ix[a], ib = ix[b];
+            const int32_t ia = staged ? s_ix[a] : ix[a], ib = staged ? s_ix[b] : ix[b];
             const T xab = dv[a] * dv[b];
             for (int c = 0; c < C; ++c) {
                 const T* pa = A.v + ((int64_t)ia * C + c) * k;
                 const T* pb = A.v + ((int64_t)ib * C + c) * k;
                 T dot = T(0);
-                for (int t = 0; t < k; ++t) dot += pa[t] * pb[t];
+                for (int t = 0; t < k; t += VEC) {
+                    const Vec<T, VEC> qa = ldg_vec<T, VEC>(pa + t), qb = ldg_vec<T, VEC>(pb + t);
+#pragma unroll
+                    for (int u = 0; u < VEC; ++u) dot += qa.v[u] * qb.v[u];
+                }
                 A.pay2[(int64_t)A.inv2[A.seg2 + e2 + pi] * A.W2 + c] = gs[c] * xab * dot;
             }
             b += 32;
