@@ -28,6 +28,8 @@
 // Kernels: train_opt.cuh (optimizer, launch order), train_plan.cuh (plan),
 // train_forward.cuh (forward), train_payload.cuh, train_tab.cuh (reductions).
 #include <algorithm>
+#include <chrono>
+#include <thread>
 #include <cstring>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -41,6 +43,11 @@
 struct mfm_dp {
     ncclComm_t comm;
     int world, rank, device;
+    // batches whose cross-rank sum has completed, written by the device into
+    // mapped host memory (the host's liveness view of the group)
+    unsigned* prog_h;
+    unsigned* prog_d;
+    bool aborted;  // the communicator was aborted after a failure
 };
 
 namespace mfm {
@@ -125,6 +132,8 @@ struct NcclApi {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
                               ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 inline const NcclApi& nccl() {
@@ -137,11 +146,13 @@ inline const NcclApi& nccl() {
         a.CommInitRank = (decltype(a.CommInitRank))dlsym(h, "ncclCommInitRank");
         a.AllReduce = (decltype(a.AllReduce))dlsym(h, "ncclAllReduce");
         a.CommDestroy = (decltype(a.CommDestroy))dlsym(h, "ncclCommDestroy");
+        a.CommAbort = (decltype(a.CommAbort))dlsym(h, "ncclCommAbort");
+        a.CommGetAsyncError = (decltype(a.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
         a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
         return a;
     }();
     if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.CommDestroy ||
-        !api.GetErrorString)
+        !api.CommAbort || !api.CommGetAsyncError || !api.GetErrorString)
         fail(MFM_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
     return api;
 }
@@ -151,6 +162,9 @@ inline const NcclApi& nccl() {
         if (r_ != ncclSuccess)                                                        \
             fail(MFM_ERR_CUDA, fmt("%s: %s", what, nccl().GetErrorString(r_)));       \
     } while (0)
+
+// Data-parallel: batches the host may enqueue ahead of the device's progress.
+constexpr uint32_t kDpAhead = 64;
 
 struct Events {
     std::vector<cudaEvent_t> e;
@@ -734,16 +748,23 @@ struct Trainer {
         if (TA.dp) {  // cross-rank sum of the batch's run sums (+ w0), then the step
             MFM_CHECK_LAUNCH("row-table reduction");
             const size_t cnt = (size_t)(TA.nrun + 1) * TA.TW;
-            MFM_NCCL(nccl().AllReduce(TA.grad, TA.grad, cnt,
-                                      sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum,
-                                      dp->comm, s),
-                     "ncclAllReduce");
+            const ncclResult_t r = nccl().AllReduce(
+                TA.grad, TA.grad, cnt, sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum,
+                dp->comm, s);
+            if (r != ncclSuccess) {  // e.g. a peer process exited: abort, then drain
+                nccl().CommAbort(dp->comm);
+                dp->aborted = true;
+                cudaStreamSynchronize(s);
+                fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group was "
+                                       "aborted", nccl().GetErrorString(r)));
+            }
             launch_pdl(fm_tab_apply_kernel<T, VW, NV>,
                        (unsigned)std::max<int64_t>(1, ceil_div(TA.nrun, 8)), 256, s, TA);
         }
         MFM_CHECK_LAUNCH("row-table reduction");
     }
-    void launch_tab(int64_t b, T inv_bsz, int64_t nrows, int64_t rlo, int64_t rhi) {
+    void launch_tab(int64_t b, T inv_bsz, int64_t nrows, int64_t rlo, int64_t rhi,
+                    uint32_t step) {
         constexpr int VW = 16 / (int)sizeof(T);
         Stream<T>& st_ = S[0];
         TabArgs<T> TA;
@@ -771,6 +792,8 @@ struct Trainer {
         TA.run0 = dp ? st_.h_run[b] : 0;
         TA.nrun = dp ? st_.h_run[b + 1] - st_.h_run[b] : 0;
         TA.grad = st_.grad.ptr;
+        TA.progress = dp ? dp->prog_d : nullptr;
+        TA.pstep = step;
         for (auto& r : TA.pre) r = L2Range{nullptr, 0};
         if (b + 1 < nb) {  // the next batch's epoch-order rows, pulled into L2 by stage 2
             const int64_t p1 = (b + 1) * B, n1 = std::min(B, n_rows - p1);
@@ -875,6 +898,44 @@ struct Trainer {
         return true;
     }
 
+    // Data-parallel liveness: wait until `target` batches have completed their
+    // cross-rank sum (the device advances dp->prog_h). A group error reported
+    // by NCCL, or no progress for MFM_B200_DP_TIMEOUT seconds (default 300),
+    // aborts the communicator, lets the stream drain and fails the call.
+    void dp_wait(uint32_t target) {
+        static const double limit = [] {
+            const char* e = getenv("MFM_B200_DP_TIMEOUT");
+            const double v = e ? atof(e) : 0.0;
+            return v > 0.0 ? v : 300.0;
+        }();
+        volatile unsigned* p = dp->prog_h;
+        unsigned last = *p;
+        auto t_last = std::chrono::steady_clock::now();
+        while ((int32_t)(*p - target) < 0) {
+            ncclResult_t st = ncclSuccess;
+            nccl().CommGetAsyncError(dp->comm, &st);
+            const unsigned cur = *p;
+            const auto now = std::chrono::steady_clock::now();
+            if (cur != last) {
+                last = cur;
+                t_last = now;
+            }
+            const bool stalled = std::chrono::duration<double>(now - t_last).count() > limit;
+            if ((st != ncclSuccess && st != ncclInProgress) || stalled) {
+                nccl().CommAbort(dp->comm);
+                dp->aborted = true;
+                cudaStreamSynchronize(s);  // the aborted collective lets the stream drain
+                if (st != ncclSuccess && st != ncclInProgress)
+                    fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group "
+                                           "was aborted", nccl().GetErrorString(st)));
+                fail(MFM_ERR_CUDA, fmt("data-parallel group: no batch completed for %.0f s (a "
+                                       "peer is not answering); the group was aborted",
+                                       limit));
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(100));
+        }
+    }
+
     // Row-table path: each epoch's plan runs in windows of batches (one event
     // per window) on the plan stream, the batches on a high-priority stream
     // forked from and joined back to s.
@@ -904,6 +965,12 @@ struct Trainer {
         MFM_CUDA(cudaStreamWaitEvent(hi, ev_fork, 0), "event");
         s = hi;
         pt.s = hi;
+        uint32_t gstep = 0;  // batches enqueued in this call
+        if (dp) {
+            if (dp->aborted)
+                fail(MFM_ERR_INVALID, "the data-parallel group was aborted; create a new one");
+            *(volatile unsigned*)dp->prog_h = 0u;
+        }
         try {
             for (int64_t e = 0; e < E; ++e) {
                 plan_tab_epoch(S[0], (int)e);
@@ -918,6 +985,11 @@ struct Trainer {
                 for (size_t w = 0; w < win.size(); ++w) {
                     MFM_CUDA(cudaStreamWaitEvent(hi, ev.e[w], 0), "event");
                     for (int64_t b = win[w].first; b < win[w].second; ++b) {
+                        // data-parallel: stay at most kDpAhead batches ahead of the
+                        // device, so a stalled group is noticed here, never inside
+                        // a launch blocked on a full queue
+                        ++gstep;
+                        if (dp && gstep > kDpAhead) dp_wait(gstep - kDpAhead);
                         const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                         const T inv_bsz = T(1) / (T)nrows;  // batch length (fm.rs:395-398)
                         // data-parallel: this rank scores rows [rlo, rhi) of the batch
@@ -940,9 +1012,10 @@ struct Trainer {
                             A.pre[2] = L2Range{S[0].rx.ptr + sg, ne * (int64_t)sizeof(T)};
                         }
                         launch_forward(A, rhi - rlo);
-                        launch_tab(b, inv_bsz, nrows, rlo, rhi);
+                        launch_tab(b, inv_bsz, nrows, rlo, rhi, gstep);
                     }
                 }
+                if (dp) dp_wait(gstep);  // the epoch's last batch, before the next plan
                 pt.mark("batches");
             }
         } catch (...) {
@@ -1358,9 +1431,21 @@ extern "C" int mfm_dp_create(const unsigned char id[128], int world, int rank, i
         DeviceGuard guard(device);
         ncclUniqueId u;
         memcpy(&u, id, sizeof(u));
+        unsigned* h = nullptr;
+        unsigned* dptr = nullptr;
+        MFM_CUDA(cudaHostAlloc(&h, sizeof(unsigned), cudaHostAllocMapped), "progress word");
+        *h = 0u;
+        if (cudaHostGetDevicePointer(&dptr, h, 0) != cudaSuccess) {
+            cudaFreeHost(h);
+            fail(MFM_ERR_CUDA, "mapped progress word unavailable");
+        }
         ncclComm_t c = nullptr;
-        MFM_NCCL(nccl().CommInitRank(&c, world, u, rank), "ncclCommInitRank");
-        *out = new mfm_dp{c, world, rank, device};
+        const ncclResult_t r = nccl().CommInitRank(&c, world, u, rank);
+        if (r != ncclSuccess) {
+            cudaFreeHost(h);
+            fail(MFM_ERR_CUDA, fmt("ncclCommInitRank: %s", nccl().GetErrorString(r)));
+        }
+        *out = new mfm_dp{c, world, rank, device, h, dptr, false};
     });
 }
 
@@ -1369,8 +1454,10 @@ extern "C" int mfm_dp_destroy(mfm_dp* dp) {
         if (!dp) return;
         DeviceGuard guard(dp->device);
         const ncclComm_t c = dp->comm;
+        const bool aborted = dp->aborted;  // an aborted communicator is already released
+        cudaFreeHost(dp->prog_h);
         delete dp;
-        MFM_NCCL(nccl().CommDestroy(c), "ncclCommDestroy");
+        if (!aborted) MFM_NCCL(nccl().CommDestroy(c), "ncclCommDestroy");
     });
 }
 

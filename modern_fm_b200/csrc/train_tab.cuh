@@ -55,6 +55,8 @@ struct TabArgs {
     int64_t run0, nrun;    // this batch's runs: [run0, run0 + nrun)
     T* grad;
     L2Range pre[5];        // the next batch's epoch-order rows, for its forward
+    unsigned* progress;    // data-parallel: mapped host word, set to pstep by the apply
+    unsigned pstep;
 };
 
 // float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
@@ -327,8 +329,10 @@ __global__ void __launch_bounds__(256) fm_tab_apply_kernel(TabArgs<T> A) {
     const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint32_t key = j < A.nrun ? A.rkey[A.run0 + j] : 0u;  // plan data
     pdl_wait();  // grad is the cross-rank sum
-    if (blockIdx.x == 0 && threadIdx.x == 0)
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
         opt_step(A.gw0, 0, A.grad[A.nrun * A.TW] * A.inv_bsz, A.opt);
+        if (A.progress) *(volatile unsigned*)A.progress = A.pstep;  // the sum has arrived
+    }
     if (j >= A.nrun) return;
     const T* gd = A.grad + j * A.TW;
     if (lane < NV) {

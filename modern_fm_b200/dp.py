@@ -10,10 +10,15 @@ no multi-GPU training; the single-GPU semantics it defines are
 rust/src/fm.rs:373-411 (batch loop) and rust/src/optimizer.rs:48-167 (steps).
 
     import torch.distributed as dist
-    dist.init_process_group("gloo")            # any backend: it only carries the group id
-    group = DataParallelGroup(device=local_rank)
+    dist.init_process_group("gloo")            # any backend: it carries the group id and
+    group = DataParallelGroup(device=local_rank)  # the peer check before each fit
     group.fm_fit_device(...)                    # every rank, same arguments
     group.close()
+
+A rank that has left is found by the bounded barrier before each fit; a rank
+lost during a fit stops the device's progress, and the engine aborts the NCCL
+communicator after MFM_B200_DP_TIMEOUT seconds (the call returns an error and
+the group must be recreated).
 """
 
 from __future__ import annotations
@@ -54,6 +59,24 @@ def broadcast_unique_id(id_bytes: bytes | None, group=None) -> bytes:
     return bytes(buf.numpy().tobytes())
 
 
+def check_peers(timeout_s: float = 60.0, group=None) -> None:
+    """Every rank of the torch.distributed group is still there: a bounded
+    barrier (gloo: monitored_barrier, which names the missing ranks; other
+    backends: barrier under the group's own timeout). Raises RuntimeError
+    instead of letting the next NCCL collective wait for a rank that left."""
+    import datetime
+
+    import torch.distributed as dist
+
+    try:
+        if dist.get_backend(group) == "gloo":
+            dist.monitored_barrier(group, timeout=datetime.timedelta(seconds=timeout_s))
+        else:
+            dist.barrier(group)
+    except Exception as exc:  # the backends raise several types
+        raise RuntimeError(f"data-parallel group: a peer is missing ({exc})") from exc
+
+
 def new_unique_id() -> bytes:
     out = ct.create_string_buffer(ID_BYTES)
     if _lib.lib().mfm_dp_unique_id(out) != 0:
@@ -70,6 +93,7 @@ class DataParallelGroup:
 
         import torch.distributed as dist
 
+        self._group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.device = int(os.environ.get("LOCAL_RANK", "0")) if device is None else int(device)
@@ -84,10 +108,15 @@ class DataParallelGroup:
         return self._h
 
     def fm_fit_device(self, dtype, indptr, indices, data, n_rows, n_features, y, sample_weight,
-                      row_orders, train, k, w0, w, v, stream):
+                      row_orders, train, k, w0, w, v, stream, check_peers_s: float | None = 60.0):
         """mfm_fm_fit_device_dp: device pointers (ints) in the compute dtype,
         `train` an _lib.Train, w0/w/v _lib.DevGroup; raises RuntimeError with
-        the engine's message on failure."""
+        the engine's message on failure. First checks that every rank is still
+        present (check_peers, skipped with check_peers_s=None); during the fit
+        the engine aborts the group if no batch completes for
+        MFM_B200_DP_TIMEOUT seconds."""
+        if check_peers_s is not None:
+            check_peers(check_peers_s, self._group)
         rc = _lib.lib().mfm_fm_fit_device_dp(self._h, dtype, indptr, indices, data, n_rows,
                                              n_features, y, sample_weight, row_orders, train, k,
                                              w0, w, v, stream)

@@ -72,3 +72,39 @@ def test_group_arguments_are_checked_before_nccl():
                                 None, tr, 4, g, g, g, None)
     assert rc == _lib.MFM_ERR_INVALID and "group" in _lib.last_error()
     assert L.mfm_dp_destroy(None) == 0
+
+
+def _peer_worker(rank, world, port, leave, out_dir):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    if leave and rank == 1:
+        os._exit(0)  # leaves between steps, nothing in flight
+    try:
+        dp.check_peers(timeout_s=3.0)
+        res = "ok"
+    except RuntimeError as exc:
+        res = "error: " + str(exc)
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(res)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("leave", [False, True])
+def test_missing_peer_is_found_before_the_next_collective(leave):
+    """The bounded barrier before each data-parallel fit passes with every rank
+    present and raises (naming the group failure) when rank 1 has left."""
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.spawn(_peer_worker, args=(2, _free_port(), leave, d), nprocs=2, join=False)
+        for _ in range(4):  # join() returns after each process; bounded overall
+            if ctx.join(30):
+                break
+        with open(os.path.join(d, "r0.txt")) as f:
+            got = f.read()
+    if leave:
+        assert got.startswith("error: data-parallel group: a peer is missing"), got
+    else:
+        assert got == "ok"

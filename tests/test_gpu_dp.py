@@ -27,7 +27,7 @@ def _data():
     return X, y, sw, V, ro
 
 
-def _fit(opt, device, group=None):
+def _fit(opt, device, group=None, **fit_kw):
     import torch
 
     from modern_fm_b200 import _lib
@@ -52,7 +52,7 @@ def _fit(opt, device, group=None):
         rc = _lib.lib().mfm_fm_fit_device(args[0], device, *args[1:])
         assert rc == 0, _lib.last_error()
     else:
-        group.fm_fit_device(*args)
+        group.fm_fit_device(*args, **fit_kw)
     torch.cuda.synchronize(dev)
     return {n: a.cpu().numpy() for n, a in (("w0", w0), ("w", w), ("V", V),
                                             ("acc_w", state[1]), ("acc_V", state[2]))}
@@ -101,3 +101,50 @@ def test_two_gpu_data_parallel_fit(opt):
     for key in keys:
         np.testing.assert_allclose(ranks[0][key], one[key], rtol=1e-7, atol=1e-9, err_msg=key)
     assert np.abs(ranks[0]["V"] - _data()[3]).max() > 1e-4  # training moved the factors
+
+
+def _lost_peer_worker(rank, world, port, out_dir):
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from modern_fm_b200 import dp
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      MFM_B200_DP_TIMEOUT="5")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    group = dp.DataParallelGroup(device=rank)
+    if rank == 1:
+        os._exit(0)  # leaves between steps: none of its kernels or collectives in flight
+    t0 = time.time()
+    try:  # no host-side peer check: the engine's own progress timeout must end the fit
+        _fit("adagrad", rank, group, check_peers_s=None)
+        res = "no error"
+    except RuntimeError as exc:
+        res = "error: " + str(exc)
+    with open(os.path.join(out_dir, "r0.txt"), "w") as f:
+        f.write(f"{res} | {time.time() - t0:.1f}")
+    group.close()
+    os._exit(0)
+
+
+def test_lost_peer_aborts_the_group_with_an_error():
+    """A rank that leaves between steps stops the group's progress; the other
+    rank's fit aborts the communicator after MFM_B200_DP_TIMEOUT (5 s) and
+    raises instead of waiting forever."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.spawn(_lost_peer_worker, args=(2, _free_port(), d), nprocs=2, join=False)
+        for _ in range(6):
+            if ctx.join(30):
+                break
+        with open(os.path.join(d, "r0.txt")) as f:
+            res, secs = f.read().rsplit(" | ", 1)
+    assert res.startswith("error: data-parallel group"), res
+    assert float(secs) < 120
