@@ -60,6 +60,13 @@ __device__ __forceinline__ void pdl_trigger() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// gr / sqrt(a) for AdaGrad: float32 through the hardware reciprocal square
+// root (rsqrtf, at most 2 ulp from the correctly rounded value, one
+// instruction instead of a rounded square root and a rounded division);
+// float64 correctly rounded.
+__device__ __forceinline__ float adagrad_scale(float gr, float a) { return gr * rsqrtf(a); }
+__device__ __forceinline__ double adagrad_scale(double gr, double a) { return gr / sqrt(a); }
+
 // One step of the reference's step_param / step_coord (rust/src/optimizer.rs:
 // 48-167) for coordinate idx of group g with batch-mean data gradient dg.
 template <class T>
@@ -75,7 +82,7 @@ __device__ __forceinline__ void opt_step(const GroupDev<T>& g, int64_t idx, T dg
         const T gr = dg + l2 * th;
         const T a = g.acc[idx] + gr * gr;
         g.acc[idx] = a;
-        th -= lr * gr / sqrt(a + (T)1e-10);
+        th -= lr * adagrad_scale(gr, a + (T)1e-10);
         break;
     }
     case MFM_OPT_ADAM: {  // adam_step, optimizer.rs:68-85 (lazy, per-coordinate t)
@@ -162,7 +169,7 @@ struct VecStep {
                 const T gr = dg[u] + l2 * th;
                 const T ac = a.v[u] + gr * gr;
                 a.v[u] = ac;
-                th -= lr * gr / sqrt(ac + (T)1e-10);
+                th -= lr * adagrad_scale(gr, ac + (T)1e-10);
                 break;
             }
             case MFM_OPT_ADAM: {

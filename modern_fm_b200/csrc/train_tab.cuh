@@ -12,10 +12,14 @@ namespace mfm {
 // Binary FM with k = NV * VEC (16-byte vectors, NV <= 8). The forward writes
 // one table row per batch row, [S (k) | g | pad], S = sum_j V_j x_j the row's
 // factor sum and g = dL/ds x sample weight. The reduction reads the batch's
-// sorted entry stream (key, row, x) and recomputes each entry's gradient from
-// the table exactly as FmGradAccum::add_row forms it (rust/src/fm.rs:136-146):
+// sorted entry stream (key, row, x). Each entry's gradient is the one
+// FmGradAccum::add_row forms (rust/src/fm.rs:136-146),
 //   gv[t] = g (x S[t] - V[t] x x),   gw = g x,
-// so no per-entry payload is ever written.
+// and V is the same row for every entry of a key's run, so the run's sum is
+//   sum gv[t] = sum (g x S[t]) - V[t] sum (g x x):
+// the reduction sums [g x S (k) | g x | g x x] from the table alone (no
+// per-entry latent-row load, no per-entry payload written) and the step that
+// owns the run subtracts V times the last column.
 //
 // Stage 1: one block per chunk of kChunk consecutive sorted entries, one
 // entry per thread; a segmented shuffle reduction per warp, then the warps'
@@ -45,9 +49,9 @@ struct TabArgs {
     GroupDev<T> gv, gw, gw0;
     OptDev opt;
     // data-parallel batch (dp != 0): this rank scores rows [rlo, rhi) of the
-    // batch; per-run sums go to grad (run - run0, stride TW; row nrun = w0)
-    // instead of the optimizer, which fm_tab_apply_kernel runs after the
-    // cross-rank sum
+    // batch; per-run sums [g x S | g x | g x x] go to grad (run - run0,
+    // stride TW; row nrun = w0) instead of the optimizer, which
+    // fm_tab_apply_kernel runs after the cross-rank sum
     int dp;
     uint32_t rlo, rhi;
     const int64_t* runs;   // per sorted entry: runs (distinct keys) before it in the epoch
@@ -67,7 +71,7 @@ constexpr int tab_min_blocks() {
 
 template <class T, int VEC, int NV, int OPT>
 __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab_reduce_kernel(TabArgs<T> A) {
-    constexpr int K = VEC * NV, NVAL = K + 1, NW = kChunk / 32;
+    constexpr int K = VEC * NV, NVAL = K + 2, NW = kChunk / 32;
     __shared__ __align__(16) T wpart[NW][NVAL];
     __shared__ int wflag[NW];  // bit 0: lane 0 continues the previous warp; bit 1: one segment
     __shared__ uint32_t s_last;
@@ -104,18 +108,17 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
     T val[NVAL];
     // data-parallel: rows of other ranks' slices add nothing here
     const bool mine = valid && (!A.dp || (row >= A.rlo && row < A.rhi));
-    if (mine) {
+    if (mine) {  // [g x S | g x | g x x]
         const T* tr = A.tab + (int64_t)row * A.TW;
-        const T* vp = A.gv.p + (int64_t)key * K;
-        const T g = tr[K];
+        const T gx = tr[K] * x;
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             const Vec<T, VEC> sv = ldg_vec<T, VEC>(tr + v * VEC);
-            const Vec<T, VEC> vk = ldg_vec<T, VEC>(vp + v * VEC);
 #pragma unroll
-            for (int u = 0; u < VEC; ++u) val[v * VEC + u] = g * (x * sv.v[u] - vk.v[u] * x * x);
+            for (int u = 0; u < VEC; ++u) val[v * VEC + u] = gx * sv.v[u];
         }
-        val[K] = g * x;
+        val[K] = gx;
+        val[K + 1] = gx * x;
     } else {
 #pragma unroll
         for (int q = 0; q < NVAL; ++q) val[q] = T(0);
@@ -165,6 +168,7 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
             *reinterpret_cast<Vec<T, VEC>*>(dst + v * VEC) = o;
         }
         dst[K] = val[K];
+        dst[K + 1] = val[K + 1];
         return;
     }
     if (A.dp) {  // the run's sum for this rank, stepped after the cross-rank sum
@@ -177,6 +181,7 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
             *reinterpret_cast<Vec<T, VEC>*>(gd + v * VEC) = o;
         }
         gd[K] = val[K];
+        gd[K + 1] = val[K + 1];
         return;
     }
     // the whole run lies in this chunk: one optimizer step per coordinate
@@ -189,7 +194,8 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
     for (int v = 0; v < NV; ++v) {
         T dg[VEC];
 #pragma unroll
-        for (int u = 0; u < VEC; ++u) dg[u] = val[v * VEC + u] * A.inv_bsz;
+        for (int u = 0; u < VEC; ++u)
+            dg[u] = (val[v * VEC + u] - st[v].p.v[u] * val[K + 1]) * A.inv_bsz;
         st[v].commit(A.gv, (int64_t)key * K + v * VEC, dg, A.opt);
     }
     const T dgw = val[K] * A.inv_bsz;
@@ -257,12 +263,12 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
         else if (lane == NV)
             s1.prefetch(A.gw, (int64_t)key, A.opt.kind);
     }
-    T tot[K + 1];
+    T tot[K + 2];
 #pragma unroll
-    for (int q = 0; q <= K; ++q) tot[q] = T(0);
+    for (int q = 0; q < K + 2; ++q) tot[q] = T(0);
     for (int64_t e0 = 0; e0 < cnt; e0 += 32) {
         const int64_t e = e0 + lane;
-        T part[K + 1];
+        T part[K + 2];
         if (e < cnt) {
             const T* r = e == 0 ? A.pt + (c - 1) * A.TW : A.ph + (c + e - 1) * A.TW;
 #pragma unroll
@@ -272,16 +278,17 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
                 for (int u = 0; u < VEC; ++u) part[v * VEC + u] = x.v[u];
             }
             part[K] = r[K];
+            part[K + 1] = r[K + 1];
         } else {
 #pragma unroll
-            for (int q = 0; q <= K; ++q) part[q] = T(0);
+            for (int q = 0; q < K + 2; ++q) part[q] = T(0);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-            for (int q = 0; q <= K; ++q) part[q] += __shfl_xor_sync(FULL, part[q], o);
+            for (int q = 0; q < K + 2; ++q) part[q] += __shfl_xor_sync(FULL, part[q], o);
 #pragma unroll
-        for (int q = 0; q <= K; ++q) tot[q] += part[q];
+        for (int q = 0; q < K + 2; ++q) tot[q] += part[q];
     }
     if (A.dp) {  // the run's sum for this rank (its head entry lies before chunk c)
         T* gd = A.grad + (A.runs[A.seg + c * kChunk] - 1 - A.run0) * A.TW;
@@ -298,6 +305,7 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
             *reinterpret_cast<Vec<T, VEC>*>(gd + lane * VEC) = o;
         } else if (lane == NV) {
             gd[K] = tot[K];
+            gd[K + 1] = tot[K + 1];
         }
         return;
     }
@@ -309,7 +317,7 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
 #pragma unroll
             for (int v = 0; v < NV; ++v)
                 if (v == own) t = tot[v * VEC + u];
-            dg[u] = t * A.inv_bsz;
+            dg[u] = (t - st.p.v[u] * tot[K + 1]) * A.inv_bsz;
         }
         st.commit(A.gv, (int64_t)key * K + lane * VEC, dg, A.opt);
     } else if (lane == NV) {
@@ -340,9 +348,10 @@ __global__ void __launch_bounds__(256) fm_tab_apply_kernel(TabArgs<T> A) {
         VecStep<T, VEC> st;
         st.prefetch(A.gv, idx0, A.opt.kind);
         const Vec<T, VEC> g = ldg_vec<T, VEC>(gd + lane * VEC);
+        const T gxx = gd[K + 1];
         T dg[VEC];
 #pragma unroll
-        for (int u = 0; u < VEC; ++u) dg[u] = g.v[u] * A.inv_bsz;
+        for (int u = 0; u < VEC; ++u) dg[u] = (g.v[u] - st.p.v[u] * gxx) * A.inv_bsz;
         st.commit(A.gv, idx0, dg, A.opt);
     } else if (lane == NV) {
         VecStep<T, 1> s1;
