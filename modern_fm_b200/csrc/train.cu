@@ -18,8 +18,8 @@
 // segmented stable radix sort by key within each batch (segsort.cuh). Then,
 // per batch, no float atomics anywhere (bitwise reproducible run to run):
 //   binary FM, k = 1/2/4/8 16-byte vectors (train_tab.cuh): the forward writes
-//     one row-table line per row [S | g]; stage 1 recomputes each sorted
-//     entry's gradient from the table, reduces segments and steps the
+//     one row-table line per row (S) and the row's g; stage 1 recomputes each
+//     sorted entry's gradient from them, reduces segments and steps the
 //     optimizer; stage 2 folds runs that cross chunk boundaries and steps w0;
 //   every other shape (train_payload.cuh): the forward writes each entry's
 //     gradient payload to its sorted position; stage 1 sums work items of
@@ -207,7 +207,7 @@ struct Stream {
     // binary FM row-table path: sorted (key, row, x) entries, the row table
     // and the chunk partials
     bool tab = false;
-    int TW = 0;
+    int TW = 0;  // row stride of ph, pt and grad (k + 16 bytes)
     DevBuf<uint32_t> erow, pidx;  // pidx: keys in epoch entry order (CSR indices by position)
     DevBuf<T> ex, rx, table, ph, pt, py, psw;
     uint32_t* rrow = nullptr;
@@ -580,7 +580,7 @@ struct Trainer {
             (nvw == 1 || nvw == 2 || nvw == 4 || nvw == 8)) {
             s0.tab = true;
             s0.TW = (int)k + VW;
-            s0.table.alloc(device, std::max<int64_t>(1, std::min(B, n_rows)) * s0.TW);
+            s0.table.alloc(device, std::max<int64_t>(1, std::min(B, n_rows)) * k);
         }
         int co = 0;
         MFM_CUDA(cudaDeviceGetAttribute(&co, cudaDevAttrCooperativeLaunch, device), "attribute");
@@ -611,7 +611,7 @@ struct Trainer {
         A.fid = p_fid;
         A.grow = grow.ptr;
         A.tab = s0.table.ptr;
-        A.TW = s0.TW;
+        A.TW = (int)k;  // row table: S only (g is in grow)
         p_data = data;
         p_y = yv;
         p_sw = swv;

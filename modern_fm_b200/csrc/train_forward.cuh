@@ -35,7 +35,7 @@ struct FwdArgs {
     int W2;
     T* grow;  // (nrows, C) per-row loss gradients, summed into the w0 gradient
     L2Range pre[3];  // row-table path: stage 1's sorted (key, row, x) of this batch
-    T* tab;   // row table (nrows, TW): [S (k) | g | pad] (binary FM row-table path)
+    T* tab;   // row table (nrows, TW = k): S per row (binary FM row-table path; g in grow)
     int TW;
 };
 
@@ -257,7 +257,7 @@ __device__ __forceinline__ void rows_payload(const FwdArgs<T>& A, int64_t e0, in
     }
 }
 
-// TAB: write the row table [S | g] instead of per-entry payloads.
+// TAB: write the row table (S) and g instead of per-entry payloads.
 template <class T, int VEC, int L, int LR, int CAP, bool TAB = false>
 __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t slot0,
                                                     int64_t nslots) {
@@ -326,7 +326,6 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
                     for (int u = 0; u < VEC; ++u) o.v[u] = cache[u];
                     *reinterpret_cast<Vec<T, VEC>*>(tr + l * VEC) = o;
                 }
-                if (rl == 0) tr[A.k] = g;
             }
             continue;
         }

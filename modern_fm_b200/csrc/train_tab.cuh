@@ -10,8 +10,9 @@ namespace mfm {
 // ------------------------------------------ binary FM row-table reduction --
 //
 // Binary FM with k = NV * VEC (16-byte vectors, NV <= 8). The forward writes
-// one table row per batch row, [S (k) | g | pad], S = sum_j V_j x_j the row's
-// factor sum and g = dL/ds x sample weight. The reduction reads the batch's
+// one table row per batch row, S (k) = sum_j V_j x_j the row's factor sum
+// (rows of k elements: whole 32-byte sectors), and the row's
+// g = dL/ds x sample weight into grow (4096 values, held in L1). The reduction reads the batch's
 // sorted entry stream (key, row, x). Each entry's gradient is the one
 // FmGradAccum::add_row forms (rust/src/fm.rs:136-146),
 //   gv[t] = g (x S[t] - V[t] x x),   gw = g x,
@@ -38,13 +39,13 @@ struct TabArgs {
     const uint32_t* keys;  // sorted keys of the epoch's entry stream
     const uint32_t* rrow;  // batch-local row of each sorted entry
     const T* rx;           // value of each sorted entry
-    const T* tab;          // (nrows, TW) [S | g | pad]
+    const T* tab;          // (nrows, k) S per row
     T* ph;                 // (chunks, TW) sums continued from the previous chunk
     T* pt;                 // (chunks, TW) sums continued into the next chunk
     int TW;
     int64_t seg, n;        // this batch's entries: [seg, seg + n) of the sorted stream
     int64_t nrows;
-    const T* grow;         // per-row g, for w0
+    const T* grow;         // per-row g (the entries' g, and w0's)
     T inv_bsz;
     GroupDev<T> gv, gw, gw0;
     OptDev opt;
@@ -109,8 +110,8 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
     // data-parallel: rows of other ranks' slices add nothing here
     const bool mine = valid && (!A.dp || (row >= A.rlo && row < A.rhi));
     if (mine) {  // [g x S | g x | g x x]
-        const T* tr = A.tab + (int64_t)row * A.TW;
-        const T gx = tr[K] * x;
+        const T* tr = A.tab + (int64_t)row * K;
+        const T gx = __ldg(A.grow + row) * x;
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             const Vec<T, VEC> sv = ldg_vec<T, VEC>(tr + v * VEC);
