@@ -11,7 +11,9 @@
 // Stability makes the final order (key, original position) — deterministic,
 // with no floating point involved. The last pass can replace each value by
 // data gathered through it (RecGather): the sorted stream then carries what
-// its consumer reads instead of an index into the unsorted one.
+// its consumer reads instead of an index into the unsorted one. When the
+// values to sort are the entries' segment-relative positions, the first pass
+// generates them (IOTA) instead of reading them.
 #pragma once
 
 #include <algorithm>
@@ -72,17 +74,24 @@ struct PlainValue {
         vout[dst] = p.v;
     }
 };
+// A (row, value) record, packed so one gather reads one sector: 8 bytes for
+// float, 16 for double.
+template <class T>
+struct alignas(2 * sizeof(T)) RowVal {
+    uint32_t row;
+    T x;
+};
 template <class T>
 struct RecGather {
-    const uint32_t* a;  // -> vout
-    const T* b;         // -> bout
+    const RowVal<T>* a;  // row -> vout, value -> bout
     T* bout;
     struct P {
         uint32_t v;
         T x;
     };
     __device__ __forceinline__ P load(int64_t seg0, uint32_t val) const {
-        return P{__ldg(a + seg0 + val), __ldg(b + seg0 + val)};
+        const RowVal<T> r = a[seg0 + val];
+        return P{r.row, r.x};
     }
     __device__ __forceinline__ void store(uint32_t* vout, int64_t dst, const P& p) const {
         vout[dst] = p.v;
@@ -97,7 +106,7 @@ struct RecGather {
 // digit and over the digits gives each key its stable tile-local position.
 // The tile is reordered by digit in shared memory, then written out: every
 // digit's keys form one contiguous run of the output, so the stores coalesce.
-template <class Out>
+template <class Out, bool IOTA = false>
 __global__ void __launch_bounds__(kSortNT)
     seg_scatter_kernel(const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin,
                        uint32_t* __restrict__ kout, uint32_t* __restrict__ vout,
@@ -122,7 +131,7 @@ __global__ void __launch_bounds__(kSortNT)
     for (int i = 0; i < kSortItems; ++i) {
         const int q = q0 + i * 32;
         key[i] = q < n ? kt[q] : 0u;
-        val[i] = q < n ? vt[q] : 0u;
+        val[i] = IOTA ? (uint32_t)(lo - seg0) + (uint32_t)q : (q < n ? vt[q] : 0u);
     }
     __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
@@ -303,11 +312,14 @@ inline void build_sort_tiles(int device, cudaStream_t s, const std::vector<int64
 }
 
 // segmented_sort restricted to segments [b0, b1) with the epoch tile table T;
-// no host synchronisation. Same buffer rules as segmented_sort.
+// no host synchronisation. Same buffer rules as segmented_sort. With iota,
+// the values are each entry's position relative to its segment start: the
+// first pass generates them and v0 is not read.
 template <class Last = PlainValue>
 SortResult segmented_sort_range(cudaStream_t s, const uint32_t* kfirst, uint32_t* k0, uint32_t* v0,
                                 uint32_t* k1, uint32_t* v1, const int64_t* d_seg_lo, int64_t b0,
-                                int64_t b1, SortTiles& T, int key_bits, Last last = Last{}) {
+                                int64_t b1, SortTiles& T, int key_bits, Last last = Last{},
+                                bool iota = false) {
     SortResult res{k0, v0};
     constexpr bool gather = !std::is_same<Last, PlainValue>::value;
     if (gather && key_bits < 1) key_bits = 1;
@@ -323,12 +335,21 @@ SortResult segmented_sort_range(cudaStream_t s, const uint32_t* kfirst, uint32_t
         for (int shift = 0; shift < key_bits; shift += 8) {
             seg_hist_kernel<<<nt, 256, 0, s>>>(ki, tlo, thi, shift, hist);
             seg_offsets_kernel<<<ns, 256, 0, s>>>(d_seg_lo + b0, T.seg_tile.ptr + b0, T.hist.ptr);
-            if (gather && shift + 8 >= key_bits)
-                seg_scatter_kernel<Last><<<nt, kSortNT, 0, s>>>(ki, vi, ko, vo, tlo, thi, tsg,
-                                                                shift, hist, last);
-            else
+            const bool gen = iota && shift == 0;
+            if (gather && shift + 8 >= key_bits) {
+                if (gen)
+                    seg_scatter_kernel<Last, true><<<nt, kSortNT, 0, s>>>(
+                        ki, vi, ko, vo, tlo, thi, tsg, shift, hist, last);
+                else
+                    seg_scatter_kernel<Last><<<nt, kSortNT, 0, s>>>(ki, vi, ko, vo, tlo, thi,
+                                                                    tsg, shift, hist, last);
+            } else if (gen) {
+                seg_scatter_kernel<PlainValue, true><<<nt, kSortNT, 0, s>>>(
+                    ki, vi, ko, vo, tlo, thi, tsg, shift, hist, PlainValue{});
+            } else {
                 seg_scatter_kernel<PlainValue><<<nt, kSortNT, 0, s>>>(
                     ki, vi, ko, vo, tlo, thi, tsg, shift, hist, PlainValue{});
+            }
             MFM_CHECK_LAUNCH("segmented sort launch");
             uint32_t* nk = ko == k1 ? k0 : k1;
             uint32_t* nv = vo == v1 ? v0 : v1;

@@ -208,7 +208,8 @@ struct Stream {
     // and the chunk partials
     bool tab = false;
     int TW = 0;  // row stride of ph, pt and grad (k + 16 bytes)
-    DevBuf<uint32_t> erow, pidx;  // pidx: keys in epoch entry order (CSR indices by position)
+    DevBuf<uint32_t> pidx;  // keys in epoch entry order (CSR indices by position)
+    DevBuf<RowVal<T>> erx;  // (batch-local row, value) per entry in epoch order
     DevBuf<T> ex, rx, table, ph, pt, py, psw;
     uint32_t* rrow = nullptr;
     SortTiles tiles;
@@ -346,7 +347,7 @@ struct Trainer {
             st_.v0.alloc(device, N1);
             st_.k1.alloc(device, N1);
             st_.v1.alloc(device, N1);
-            st_.erow.alloc(device, N1);
+            st_.erx.alloc(device, N1);
             st_.pidx.alloc(device, N1);
             st_.ex.alloc(device, N1);
             st_.rx.alloc(device, N1);
@@ -374,12 +375,12 @@ struct Trainer {
         if (p1 > p0)
             expand_kernel<T><<<warp_grid(device, p1 - p0, 8, 8), 256, 0, ps>>>(
                 FEAT, order, p_indptr, p_indices, p_fid, (int)F, p0, p1, B, st_.estart.ptr,
-                st_.seg_lo.ptr, st_.pidx.ptr, st_.v0.ptr, p_data, st_.erow.ptr, st_.ex.ptr);
+                st_.seg_lo.ptr, st_.pidx.ptr, nullptr, p_data, st_.erx.ptr, st_.ex.ptr);
         MFM_CHECK_LAUNCH("expand");
         SortResult sr = segmented_sort_range(
             ps, st_.pidx.ptr, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr, st_.seg_lo.ptr, b0,
-            b1, st_.tiles, bits_for(st_.n_keys),
-            RecGather<T>{st_.erow.ptr, st_.ex.ptr, st_.rx.ptr});
+            b1, st_.tiles, bits_for(st_.n_keys), RecGather<T>{st_.erx.ptr, st_.rx.ptr},
+            /*iota=*/true);
         st_.keys = sr.keys;  // the same buffers for every window
         st_.rrow = sr.vals;
     }
@@ -443,8 +444,8 @@ struct Trainer {
         }
         expand_kernel<T><<<warp_grid(device, n_rows, 8, 8), 256, 0, s>>>(
             st_.kind, order, p_indptr, p_indices, p_fid, (int)F, 0, n_rows, B,
-            st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr, p_data, nullptr,
-            static_cast<T*>(nullptr));
+            st_.estart.ptr, st_.seg_lo.ptr, st_.k0.ptr, st_.v0.ptr, p_data,
+            static_cast<RowVal<T>*>(nullptr), static_cast<T*>(nullptr));
         MFM_CHECK_LAUNCH("expand");
         SortResult sr = segmented_sort(device, s, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr,
                                        st_.seg_lo.ptr, nb, N, bits_for(st_.n_keys));

@@ -81,8 +81,9 @@ __device__ __forceinline__ void pair_step(int64_t& a, int64_t& b, int64_t z) {
 
 // One warp per epoch position: writes the keys and batch-local entry ids of
 // the row's entries, in the order the forward kernel writes their payloads.
-// With erow set (FEAT only), also each entry's batch-local row and value, for
-// the row-table reduction.
+// With erx set (FEAT only), instead of the ids (vals = nullptr: the sort
+// generates them), each entry's value in epoch order (ex) and its (batch-local
+// row, value) record (erx), for the row-table reduction.
 template <class T>
 __global__ void __launch_bounds__(256)
     expand_kernel(int kind, const int32_t* __restrict__ order, const int64_t* __restrict__ indptr,
@@ -90,8 +91,8 @@ __global__ void __launch_bounds__(256)
                   int64_t pos_lo, int64_t pos_hi, int64_t B, const int64_t* __restrict__ estart,
                   const int64_t* __restrict__ seg_lo, uint32_t* __restrict__ keys,
                   uint32_t* __restrict__ vals, const T* __restrict__ data,
-                  uint32_t* __restrict__ erow, T* __restrict__ ex) {
-    // (FEAT with erow: keys[] is kept unsorted as the epoch-order CSR indices)
+                  RowVal<T>* __restrict__ erx, T* __restrict__ ex) {
+    // (FEAT with erx: keys[] is kept unsorted as the epoch-order CSR indices)
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t pos = pos_lo + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
@@ -105,10 +106,11 @@ __global__ void __launch_bounds__(256)
             const uint32_t rib = (uint32_t)(pos % B);
             for (int64_t a = lane; a < z; a += 32) {
                 keys[base + a] = (uint32_t)ix[a];
-                vals[base + a] = (uint32_t)(local + a);
-                if (erow) {
-                    erow[base + a] = rib;
-                    ex[base + a] = data[rb + a];
+                if (vals) vals[base + a] = (uint32_t)(local + a);
+                if (erx) {
+                    const T xv = data[rb + a];
+                    erx[base + a] = RowVal<T>{rib, xv};
+                    ex[base + a] = xv;
                 }
             }
         } else if (kind == SLOT) {  // ordered pairs (a, b != a): key = i_a * F + f_b
