@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kSortNT)
     __shared__ uint32_t cnt[NW][256];  // per-warp digit counts -> tile-local start per warp
     __shared__ uint32_t base[256];     // output offset (segment-relative) minus tile-local start
     __shared__ uint32_t scan_sm[NW];
-    __shared__ uint32_t skey[kSortTile], sval[kSortTile];
+    __shared__ uint2 skv[kSortTile];  // (key, value), one 8-byte store per entry
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t lo = tile_lo[blockIdx.x], hi = tile_hi[blockIdx.x];
     const int64_t seg0 = tile_seg_lo[blockIdx.x];
@@ -169,21 +169,20 @@ __global__ void __launch_bounds__(kSortNT)
         if (q0 + i * 32 < n) {
             const uint32_t d = (key[i] >> shift) & 255u;
             const uint32_t lp = cnt[warp][d] + rank[i];
-            skey[lp] = key[i];
-            sval[lp] = val[i];
+            skv[lp] = make_uint2(key[i], val[i]);
         }
     __syncthreads();
     typename Out::P pay[kSortItems];
 #pragma unroll
     for (int u = 0; u < kSortItems; ++u) {
         const int j = t + u * kSortNT;
-        if (j < n) pay[u] = out.load(seg0, sval[j]);
+        if (j < n) pay[u] = out.load(seg0, skv[j].y);
     }
 #pragma unroll
     for (int u = 0; u < kSortItems; ++u) {
         const int j = t + u * kSortNT;
         if (j < n) {
-            const uint32_t k = skey[j];
+            const uint32_t k = skv[j].x;
             const int64_t dst = seg0 + (int64_t)(base[(k >> shift) & 255u] + (uint32_t)j);
             kout[dst] = k;
             out.store(vout, dst, pay[u]);
