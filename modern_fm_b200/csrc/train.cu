@@ -544,6 +544,8 @@ struct Trainer {
         opt = OptDev{c->optimizer, c->learning_rate, c->beta_1, c->beta_2, c->epsilon,
                      c->ftrl_beta, {c->l1_linear, c->l1_factors, 0.0},
                      {c->l2_linear, c->l2_factors, 0.0}};
+        opt.lb1 = std::log2(c->beta_1);
+        opt.lb2 = std::log2(c->beta_2);
         constexpr int VW = 16 / (int)sizeof(T);
         Stream<T>& s0 = S[0];
         s0.kind = FEAT;

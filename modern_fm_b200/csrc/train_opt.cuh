@@ -25,6 +25,7 @@ struct OptDev {
     int kind;
     double lr, b1, b2, eps, fbeta;
     double l1[3], l2[3];
+    double lb1, lb2;  // log2(b1), log2(b2): Adam's b^t as exp2(t log2 b)
 };
 
 // Programmatic dependent launch (sm_90+): a kernel launched with the
@@ -69,52 +70,78 @@ __device__ __forceinline__ double adagrad_scale(double gr, double a) { return gr
 
 // One step of the reference's step_param / step_coord (rust/src/optimizer.rs:
 // 48-167) for coordinate idx of group g with batch-mean data gradient dg.
+// Split in two so that a caller stepping several scalar coordinates issues
+// every coordinate's parameter and state loads before the first step.
+template <class T>
+struct CoordStep {
+    T p, a, b, c;  // param and up to three state values
+    __device__ __forceinline__ void load(const GroupDev<T>& g, int64_t idx, int kind) {
+        p = g.p[idx];
+        if (kind == MFM_OPT_ADAGRAD) {
+            a = g.acc[idx];
+        } else if (kind == MFM_OPT_ADAM) {
+            a = g.m[idx];
+            b = g.s[idx];
+            c = g.t[idx];
+        } else if (kind == MFM_OPT_FTRL) {
+            a = g.z[idx];
+            b = g.n[idx];
+        }
+    }
+    __device__ __forceinline__ void apply(const GroupDev<T>& g, int64_t idx, T dg,
+                                          const OptDev& o) {
+        T th = p;
+        const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
+        switch (o.kind) {
+        case MFM_OPT_SGD:  // apply_update, optimizer.rs:48-60
+            th -= lr * (dg + l2 * th);
+            break;
+        case MFM_OPT_ADAGRAD: {
+            const T gr = dg + l2 * th;
+            const T ac = a + gr * gr;
+            g.acc[idx] = ac;
+            th -= lr * adagrad_scale(gr, ac + (T)1e-10);
+            break;
+        }
+        case MFM_OPT_ADAM: {  // adam_step, optimizer.rs:68-85 (lazy, per-coordinate t)
+            const T gr = dg + l2 * th;
+            const T b1 = (T)o.b1, b2 = (T)o.b2;
+            const T t = c + T(1);
+            const T m = b1 * a + (T(1) - b1) * gr;
+            const T v = b2 * b + (T(1) - b2) * gr * gr;
+            g.t[idx] = t;
+            g.m[idx] = m;
+            g.s[idx] = v;
+            const T mh = m / (T(1) - exp2(t * (T)o.lb1));  // b1^t
+            const T vh = v / (T(1) - exp2(t * (T)o.lb2));  // b2^t
+            th -= lr * mh / (sqrt(vh) + (T)o.eps);
+            break;
+        }
+        default: {  // FTRL-Proximal, ftrl_step, optimizer.rs:93-105 (pure data gradient)
+            const T n = b;
+            const T nn = n + dg * dg;
+            const T sigma = (sqrt(nn) - sqrt(n)) / lr;
+            const T z = a + dg - sigma * th;
+            g.z[idx] = z;
+            g.n[idx] = nn;
+            if (fabs(z) <= l1)
+                th = T(0);
+            else {
+                const T sign = z < T(0) ? T(-1) : T(1);
+                th = -(z - sign * l1) / (((T)o.fbeta + sqrt(nn)) / lr + l2);
+            }
+        }
+        }
+        g.p[idx] = th;
+    }
+};
+
 template <class T>
 __device__ __forceinline__ void opt_step(const GroupDev<T>& g, int64_t idx, T dg,
                                          const OptDev& o) {
-    T th = g.p[idx];
-    const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
-    switch (o.kind) {
-    case MFM_OPT_SGD:  // apply_update, optimizer.rs:48-60
-        th -= lr * (dg + l2 * th);
-        break;
-    case MFM_OPT_ADAGRAD: {
-        const T gr = dg + l2 * th;
-        const T a = g.acc[idx] + gr * gr;
-        g.acc[idx] = a;
-        th -= lr * adagrad_scale(gr, a + (T)1e-10);
-        break;
-    }
-    case MFM_OPT_ADAM: {  // adam_step, optimizer.rs:68-85 (lazy, per-coordinate t)
-        const T gr = dg + l2 * th;
-        const T b1 = (T)o.b1, b2 = (T)o.b2;
-        const T t = g.t[idx] + T(1);
-        const T m = b1 * g.m[idx] + (T(1) - b1) * gr;
-        const T v = b2 * g.s[idx] + (T(1) - b2) * gr * gr;
-        g.t[idx] = t;
-        g.m[idx] = m;
-        g.s[idx] = v;
-        const T mh = m / (T(1) - pow(b1, t));
-        const T vh = v / (T(1) - pow(b2, t));
-        th -= lr * mh / (sqrt(vh) + (T)o.eps);
-        break;
-    }
-    default: {  // FTRL-Proximal, ftrl_step, optimizer.rs:93-105 (pure data gradient)
-        const T n = g.n[idx];
-        const T nn = n + dg * dg;
-        const T sigma = (sqrt(nn) - sqrt(n)) / lr;
-        const T z = g.z[idx] + dg - sigma * th;
-        g.z[idx] = z;
-        g.n[idx] = nn;
-        if (fabs(z) <= l1)
-            th = T(0);
-        else {
-            const T sign = z < T(0) ? T(-1) : T(1);
-            th = -(z - sign * l1) / (((T)o.fbeta + sqrt(nn)) / lr + l2);
-        }
-    }
-    }
-    g.p[idx] = th;
+    CoordStep<T> cs;
+    cs.load(g, idx, o.kind);
+    cs.apply(g, idx, dg, o);
 }
 
 // opt_step on VEC consecutive coordinates [idx0, idx0 + VEC) of one group,
@@ -181,8 +208,8 @@ struct VecStep {
                 c.v[u] = t;
                 a.v[u] = m;
                 b.v[u] = v;
-                const T mh = m / (T(1) - pow(b1, t));
-                const T vh = v / (T(1) - pow(b2, t));
+                const T mh = m / (T(1) - exp2(t * (T)o.lb1));  // b1^t
+                const T vh = v / (T(1) - exp2(t * (T)o.lb2));  // b2^t
                 th -= lr * mh / (sqrt(vh) + (T)o.eps);
                 break;
             }

@@ -30,12 +30,32 @@ struct RedArgs {
     GroupDev<T> gw0;
 };
 
-template <class T>
-__device__ __forceinline__ void apply_col(const RedArgs<T>& R, uint32_t key, int col, T sum) {
-    if (col < R.cb1)
-        opt_step(R.g0, (int64_t)key * R.g0.width + col, sum * R.inv_bsz, R.opt);
-    else
-        opt_step(R.g1, (int64_t)key * R.g1.width + (col - R.cb1), sum * R.inv_bsz, R.opt);
+// Steps the scalar columns [vv*VEC, vv*VEC + VEC) of key `key` (those below
+// W) with column sums `sum`: every column's loads are issued before the first
+// step, so the columns cost one memory round trip, not one each.
+template <class T, int VEC>
+__device__ __forceinline__ void apply_cols(const RedArgs<T>& R, uint32_t key, int vv,
+                                           const T* sum) {
+    CoordStep<T> cs[VEC];
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+        const int col = vv * VEC + c;
+        if (col >= R.W) continue;
+        if (col < R.cb1)
+            cs[c].load(R.g0, (int64_t)key * R.g0.width + col, R.opt.kind);
+        else
+            cs[c].load(R.g1, (int64_t)key * R.g1.width + (col - R.cb1), R.opt.kind);
+    }
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+        const int col = vv * VEC + c;
+        if (col >= R.W) continue;
+        if (col < R.cb1)
+            cs[c].apply(R.g0, (int64_t)key * R.g0.width + col, sum[c] * R.inv_bsz, R.opt);
+        else
+            cs[c].apply(R.g1, (int64_t)key * R.g1.width + (col - R.cb1), sum[c] * R.inv_bsz,
+                        R.opt);
+    }
 }
 
 // Applies one VEC-wide column vector `vv` of key `key`: 16-byte accesses when
@@ -84,18 +104,14 @@ __device__ __forceinline__ void reduce_items_dev(const RedArgs<T>& R, int64_t n_
             for (int c = 0; c < VEC; ++c) acc[c] *= R.inv_bsz;
             st.commit(R.g0, idx0, acc, R.opt);
         } else {
-#pragma unroll
-            for (int c = 0; c < VEC; ++c) {
-                const int col = vv * VEC + c;
-                if (col < R.W) apply_col(R, d.key, col, acc[c]);
-            }
+            apply_cols<T, VEC>(R, d.key, vv, acc);
         }
     }
     }
 }
 
 template <class T, int VEC>
-__global__ void __launch_bounds__(256) reduce_items_kernel(RedArgs<T> R, int64_t n_items) {
+__global__ void __launch_bounds__(256, 4) reduce_items_kernel(RedArgs<T> R, int64_t n_items) {
     reduce_items_dev<T, VEC>(R, n_items, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5,
                              ((int64_t)gridDim.x * blockDim.x) >> 5);
 }
@@ -195,11 +211,7 @@ __device__ __forceinline__ void reduce_runs_dev(const RedArgs<T>& R, int64_t l0,
                     for (int c = 0; c < VEC; ++c) tot[c] *= R.inv_bsz;
                     st.commit(R.g0, idx0, tot, R.opt);
                 } else {
-#pragma unroll
-                    for (int c = 0; c < VEC; ++c) {
-                        const int col = vv * VEC + c;
-                        if (col < R.W) apply_col(R, key, col, tot[c]);
-                    }
+                    apply_cols<T, VEC>(R, key, vv, tot);
                 }
             }
             __syncthreads();
