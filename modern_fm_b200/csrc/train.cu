@@ -678,6 +678,10 @@ struct Trainer {
                 Lc <<= 1;
                 ++lgc;
             }
+            if (D > 32 && D <= 128) {  // two nonzeros per warp step, up to 8 columns a lane
+                Lc = 16;
+                lgc = 4;
+            }
             const int mcol = (D + Lc - 1) / Lc;
             const size_t sm = (size_t)8 * (D + 3 * C) * sizeof(T);
 #define MFM_FWD(MC)                                                                   \
