@@ -766,7 +766,9 @@ struct Trainer {
                                        "aborted", nccl().GetErrorString(r)));
             }
             launch_pdl(fm_tab_apply_kernel<T, VW, NV>,
-                       (unsigned)std::max<int64_t>(1, ceil_div(TA.nrun, 8)), 256, s, TA);
+                       (unsigned)std::max<int64_t>(
+                           1, ceil_div(TA.nrun, 8 * tab_apply_runs_per_warp<NV>())),
+                       256, s, TA);
         }
         MFM_CHECK_LAUNCH("row-table reduction");
     }

@@ -327,22 +327,30 @@ __global__ void __launch_bounds__(256) fm_tab_fold_kernel(TabArgs<T> A, int64_t 
     }
 }
 
-// Data-parallel step: after the cross-rank sum of grad, one warp per run of
-// the batch applies the optimizer to its key (NV vector lanes + the w lane),
-// identically on every rank; thread 0 of block 0 also steps w0.
+// Data-parallel step: after the cross-rank sum of grad, a group of NV + 1
+// lanes per run of the batch (NV vector lanes + the w lane; 32 / (NV + 1) runs
+// per warp) applies the optimizer to its key, identically on every rank;
+// thread 0 of block 0 also steps w0.
+template <int NV>
+constexpr int tab_apply_runs_per_warp() {
+    return 32 / (NV + 1);
+}
 template <class T, int VEC, int NV>
 __global__ void __launch_bounds__(256) fm_tab_apply_kernel(TabArgs<T> A) {
-    constexpr int K = VEC * NV;
+    constexpr int K = VEC * NV, RPW = tab_apply_runs_per_warp<NV>();
     pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    const int64_t j = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int wl = threadIdx.x & 31;
+    const int lane = wl % (NV + 1);  // lane within the run's group
+    const bool spare = wl >= RPW * (NV + 1);  // lanes beyond the warp's last group
+    const int64_t j =
+        (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * RPW + (spare ? 0 : wl / (NV + 1));
     const uint32_t key = j < A.nrun ? A.rkey[A.run0 + j] : 0u;  // plan data
     pdl_wait();  // grad is the cross-rank sum
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         opt_step(A.gw0, 0, A.grad[A.nrun * A.TW] * A.inv_bsz, A.opt);
         if (A.progress) *(volatile unsigned*)A.progress = A.pstep;  // the sum has arrived
     }
-    if (j >= A.nrun) return;
+    if (spare || j >= A.nrun) return;
     const T* gd = A.grad + j * A.TW;
     if (lane < NV) {
         const int64_t idx0 = (int64_t)key * K + lane * VEC;
