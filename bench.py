@@ -405,6 +405,89 @@ def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
             "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong"}
 
 
+PREP_BYTES_PER_ENTRY = 8 + 8 + 4 + 4  # int64 + float64 read, int32 + float32 written
+PREP_BYTES_PER_ROW = 8 + 8            # indptr read and written
+
+
+def prep_measure(args, local, dev_t, L, _lib, X):
+    """Device CSR canonicalisation (mfm_csr_prep_device, the reference's
+    `_prep_csr`, python/modern_fm/_backend.py:44-52) on the scoring batch in the
+    boundary format (int64 indices, float64 values), twice: as generated
+    (already canonical: the one-pass path) and with every row reversed and its
+    middle entry's column set to its first entry's (unsorted with one duplicate
+    per row: the full path). Timed per call with CUDA events (each call ends
+    with a stream synchronisation, inside the timing); parity of the first
+    2,000 rows against the oracle."""
+    import ctypes as ct
+
+    import torch
+
+    n = X["indptr"].numel() - 1
+    ip = X["indptr"]
+    ix = X["indices"].long()
+    dv = X["data"].double()
+    nnz = ix.numel()
+    lens = ip[1:] - ip[:-1]
+    row = torch.repeat_interleave(torch.arange(n, device=dev_t), lens)
+    q = torch.arange(nnz, device=dev_t)
+    rev = ip[row] + ip[row + 1] - 1 - q
+    ix_raw, dv_raw = ix[rev].clone(), dv[rev].clone()
+    mid = ip[:-1] + lens // 2
+    has = lens > 2
+    ix_raw[mid[has]] = ix_raw[ip[:-1][has]]
+    ip_out = torch.empty(n + 1, dtype=torch.int64, device=dev_t)
+    ix_out = torch.empty(nnz, dtype=torch.int32, device=dev_t)
+    dv_out = torch.empty(nnz, dtype=torch.float32, device=dev_t)
+    stream = torch.cuda.current_stream(dev_t)
+    res = {}
+    for name, (a, b) in (("canonical", (ix, dv)), ("unsorted_dup", (ix_raw, dv_raw))):
+        m = ct.c_int64(0)
+
+        def call():
+            rc = L.mfm_csr_prep_device(_lib.MFM_DTYPE_F32, local, n, N_FEATURES, nnz,
+                                       ip.data_ptr(), a.data_ptr(), b.data_ptr(),
+                                       ip_out.data_ptr(), ix_out.data_ptr(), dv_out.data_ptr(),
+                                       ct.byref(m), stream.cuda_stream)
+            if rc:
+                raise RuntimeError(_lib.last_error())
+
+        for _ in range(3):
+            call()
+        steps = 10
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record(stream)
+        for _ in range(steps):
+            call()
+        ev[1].record(stream)
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / steps
+        algo = n * PREP_BYTES_PER_ROW + nnz * (8 + 8) + m.value * (4 + 4)
+        from oracle import oracle as O
+
+        rows = 2000
+        e = int(ip[rows].item())
+        want = O.prep_csr(ip[:rows + 1].cpu().numpy(), a[:e].cpu().numpy(), b[:e].cpu().numpy(),
+                          N_FEATURES)
+        got_ip = ip_out[:rows + 1].cpu().numpy()
+        mm = int(got_ip[-1])
+        parity = bool(np.array_equal(got_ip, want[0])
+                      and np.array_equal(ix_out[:mm].cpu().numpy().astype(np.int64), want[1])
+                      and np.array_equal(dv_out[:mm].cpu().numpy(), want[2].astype(np.float32)))
+        res[name] = {"rows_per_s": n / (ms / 1e3), "ms_per_call": ms, "nnz_in": nnz,
+                     "nnz_out": m.value, "achieved_gbs": algo / (ms / 1e3) / 1e9,
+                     "algorithmic_bytes": algo, "parity": parity}
+    peak, kind = peaks()
+    for v in res.values():
+        v["frac"] = v["achieved_gbs"] / peak
+    res["peak_gbs"], res["peak_kind"] = peak, kind
+    res["bytes"] = ("indptr 8 read + 8 written per row; per input entry int64 column + float64 "
+                    "value read; per output entry int32 column + float32 value written")
+    res["workload"] = ("the 2,000,000-row scoring batch in the boundary format (int64 / "
+                       "float64), canonical and with rows reversed plus one duplicate per row")
+    return res
+
+
 def run_ours(args):
     import torch
 
@@ -518,6 +601,7 @@ def run_ours(args):
                          f"{threads} host threads (the reference's own CPU predict is "
                          "single-threaded, rust/src/fm.rs:58-70)"}
 
+    prep = None if args.no_prep else prep_measure(args, local, dev_t, L, _lib, X)
     train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
     train_dp = (train_dp_measure(args, rank, world, local, dev_t, L, _lib)
                 if world > 1 and not args.no_train else None)
@@ -546,6 +630,8 @@ def run_ours(args):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        if prep:
+            line["prep"] = prep
         if train:
             line["train"] = train
         if train_dp:
@@ -710,6 +796,8 @@ def main():
     ap.add_argument("--train-only", action="store_true",
                     help="only the training measurement (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--no-prep", action="store_true",
+                    help="skip the device CSR canonicalisation measurement")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS)
     ap.add_argument("--train-steps", type=int, default=2)
     ap.add_argument("--train-e2e-rows", type=int, default=2_000_000)

@@ -188,6 +188,25 @@ int mfm_fwfm_predict_device(int dtype, int device, const int64_t* indptr,
                             const void* w, const void* v, const void* r, int64_t k, void* out,
                             void* stream);
 
+/* ---- device-side CSR canonicalisation ------------------------------------
+ * Replaces the host canonicalisation the reference runs before every native
+ * call, `_prep_csr` (python/modern_fm/_backend.py:44-52: float64 cast, scipy
+ * sum_duplicates, int64 / float64 copies), and the O(nnz) part of its CSR
+ * validation (CsrView::new, rust/src/data.rs:14-44). Input: a DEVICE CSR on
+ * `device` in the boundary format (indptr int64 (n_rows+1), indices int64,
+ * data float64), rows in any column order, duplicate (row, column) entries
+ * allowed. Output (caller-owned DEVICE buffers of n_rows+1 / nnz / nnz
+ * entries): the canonical CSR in the compute layout the *_device entry points
+ * take: columns sorted within each row, duplicates summed in float64 in their
+ * original order (explicit zeros kept), indices int32, data in `dtype`.
+ * *nnz_out (host) receives the canonical entry count. Invalid CSR structure or
+ * a column outside [0, n_features) returns MFM_ERR_INVALID with the
+ * reference's message. Runs on `stream` (a cudaStream_t) and synchronises it. */
+int mfm_csr_prep_device(int dtype, int device, int64_t n_rows, int64_t n_features, int64_t nnz,
+                        const int64_t* indptr, const int64_t* indices, const double* data,
+                        int64_t* indptr_out, int32_t* indices_out, void* data_out,
+                        int64_t* nnz_out, void* stream);
+
 /* ---- allocation-free FM scoring --------------------------------------------
  * No counterpart in the reference: an addition for callers that cannot let
  * the library allocate GPU memory, such as a host that owns the whole device

@@ -91,6 +91,9 @@ _SIGNATURES = {
                                         ct.c_void_p, ct.c_int64, ct.c_int64, ct.c_void_p,
                                         ct.c_void_p, ct.c_void_p, ct.POINTER(Train), ct.c_int64]
                              + [ct.POINTER(DevGroup)] * 3 + [ct.c_void_p]),
+    "mfm_csr_prep_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_int64, ct.c_int64, ct.c_int64,
+                                       ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p,
+                                       ct.c_void_p, ct.c_void_p, i64p, ct.c_void_p]),
     "mfm_fm_predict_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_double, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]),

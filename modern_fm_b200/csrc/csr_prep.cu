@@ -1,0 +1,375 @@
+// csr_prep.cu — CSR canonicalisation on the device: the step before scoring
+// and training.
+//
+// The reference canonicalises every CSR on the host before its native call:
+// `X.tocsr().astype(np.float64); X.sum_duplicates()` and int64 / float64
+// copies (python/modern_fm/_backend.py:44-52), then validates it
+// (CsrView::new, rust/src/data.rs:14-44). mfm_csr_prep_device does the same on
+// device memory and writes the engine's compute layout in one go: for a raw
+// CSR in the boundary format (int64 indptr and indices, float64 values; rows
+// in any column order, duplicate (row, column) entries allowed) it
+//   * validates indptr (starts at 0, non-decreasing, ends at nnz) and every
+//     column index against [0, n_features);
+//   * sorts each row's entries by column and sums duplicates in float64, the
+//     duplicates of one column added in their original order (explicit zeros
+//     and zero sums are kept, as scipy keeps them);
+//   * narrows to int32 columns and values in the compute dtype, so the result
+//     feeds mfm_{fm,ffm,fwfm}_predict_device and mfm_fm_fit_device directly.
+//
+// Work split (warp per row, rows grid-strided):
+//   1. csr_prep_count_kernel: one pass over the input; checks, narrows every
+//      entry in place of the output (the final result when the matrix is
+//      already canonical, the common case: nothing else runs then) and writes
+//      each row's distinct-column count. Rows of up to kShortRow entries that
+//      are out of order are counted in shared memory (first occurrences of
+//      each column); longer ones are listed for the sort.
+//   2. exclusive scan of the counts -> the output indptr.
+//   3. long unsorted rows only: their narrowed columns are gathered into one
+//      buffer and sorted stably within each row by the segmented radix sort
+//      (segsort.cuh), so equal columns keep their original order.
+//   4. csr_prep_write_kernel (rows of up to kShortRow entries and long rows
+//      already in order) and csr_prep_long_kernel (the sorted rows):
+//      each distinct column is written at its row's output offset plus its
+//      rank, with the float64 sum of its duplicates, narrowed once.
+// Every sum has a fixed order, so results are bitwise reproducible.
+#include <algorithm>
+
+#include "common.cuh"
+#include "scan.cuh"
+#include "segsort.cuh"
+
+namespace mfm {
+namespace {
+
+constexpr int kShortRow = 256;  // longest row handled in shared memory
+constexpr int kPrepWarps = 8;   // warps per block
+
+enum : unsigned {
+    kBadOrder = 1u,   // indptr decreases
+    kBadEnds = 2u,    // indptr does not start at 0 / end at nnz, or leaves [0, nnz]
+    kBadIndex = 4u,   // a column index outside [0, n_features)
+    kUnsorted = 8u,   // some row is out of order or holds duplicates
+};
+
+// flags[0]: kBad* / kUnsorted bits; flags[1]: number of long unsorted rows.
+template <class T>
+__global__ void __launch_bounds__(kPrepWarps * 32)
+    csr_prep_count_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
+                          const double* __restrict__ data, int64_t n_rows, int64_t nnz,
+                          int64_t n_features, int32_t* __restrict__ ind_out,
+                          T* __restrict__ dat_out, int64_t* __restrict__ cnt,
+                          int64_t* __restrict__ long_row, int64_t max_long, unsigned* flags) {
+    __shared__ int32_t skey[kPrepWarps][kShortRow];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
+    for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
+        const int64_t lo = indptr[r], hi = indptr[r + 1];
+        if (hi < lo || lo < 0 || hi > nnz || (r == 0 && lo != 0) ||
+            (r == n_rows - 1 && hi != nnz)) {
+            if (lane == 0) {
+                atomicOr(flags, hi < lo ? kBadOrder : kBadEnds);
+                cnt[r] = 0;
+            }
+            continue;  // warp-uniform: every lane read the same bounds
+        }
+        const int64_t len = hi - lo;
+        const bool short_row = len <= kShortRow;
+        bool unsorted = false, bad = false;
+        int64_t carry = -1;  // the previous chunk's last column
+        for (int64_t base = lo; base < hi; base += 32) {
+            const int64_t q = base + lane;
+            const bool in = q < hi;
+            const int64_t c = in ? indices[q] : 0;
+            int64_t prev = __shfl_up_sync(0xffffffffu, c, 1);
+            if (lane == 0) prev = carry;
+            bad |= in && (c < 0 || c >= n_features);
+            unsorted |= in && q > lo && !(c > prev);
+            carry = __shfl_sync(0xffffffffu, c, 31);
+            if (in) {
+                ind_out[q] = (int32_t)c;
+                dat_out[q] = (T)data[q];
+                if (short_row) skey[wib][q - lo] = (int32_t)c;
+            }
+        }
+        bad = __any_sync(0xffffffffu, bad);
+        unsorted = __any_sync(0xffffffffu, unsorted);
+        if (bad) {
+            if (lane == 0) {
+                atomicOr(flags, kBadIndex);
+                cnt[r] = 0;
+            }
+            continue;
+        }
+        int64_t count = len;
+        if (unsorted) {
+            if (short_row) {
+                __syncwarp();
+                int firsts = 0;  // entries whose column has no earlier occurrence
+                for (int e = lane; e < (int)len; e += 32) {
+                    const int32_t key = skey[wib][e];
+                    bool first = true;
+                    for (int e2 = 0; e2 < e; ++e2) first &= skey[wib][e2] != key;
+                    firsts += first;
+                }
+                count = warp_sum(firsts);
+            } else {
+                count = 0;  // counted after the sort
+                // at most nnz / (kShortRow + 1) rows fit a valid CSR; rows that
+                // overlap (a decreasing indptr, reported by another row) could
+                // list more, so the slot is bounded
+                if (lane == 0) {
+                    const unsigned slot = atomicAdd(flags + 1, 1u);
+                    if (slot < max_long) long_row[slot] = r;
+                }
+            }
+            if (lane == 0) atomicOr(flags, kUnsorted);
+        }
+        __syncwarp();  // skey is rewritten by the next row
+        if (lane == 0) cnt[r] = count;
+    }
+}
+
+// Writes rows of up to kShortRow entries, and longer rows that are already
+// strictly increasing, at their output offsets. Reads the caller's input (the
+// output arrays are being rewritten at shifted offsets by other warps).
+template <class T>
+__global__ void __launch_bounds__(kPrepWarps * 32)
+    csr_prep_write_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
+                          const double* __restrict__ data, int64_t n_rows,
+                          const int64_t* __restrict__ out_ptr, int32_t* __restrict__ ind_out,
+                          T* __restrict__ dat_out) {
+    __shared__ int32_t skey[kPrepWarps][kShortRow];
+    __shared__ double sval[kPrepWarps][kShortRow];
+    __shared__ unsigned char sfirst[kPrepWarps][kShortRow];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
+    for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
+        const int64_t lo = indptr[r], hi = indptr[r + 1], o = out_ptr[r];
+        const int64_t len = hi - lo;
+        // strictly increasing rows are copied as they are
+        bool unsorted = false;
+        int64_t carry = -1;
+        const bool short_row = len <= kShortRow;
+        // short rows are staged whole; long ones stop at the first disorder
+        for (int64_t base = lo; base < hi && (short_row || !unsorted); base += 32) {
+            const int64_t q = base + lane;
+            const int64_t c = q < hi ? indices[q] : 0;
+            int64_t prev = __shfl_up_sync(0xffffffffu, c, 1);
+            if (lane == 0) prev = carry;
+            unsorted |= __any_sync(0xffffffffu, q < hi && q > lo && !(c > prev));
+            carry = __shfl_sync(0xffffffffu, c, 31);
+            if (short_row && q < hi) {
+                skey[wib][q - lo] = (int32_t)c;
+                sval[wib][q - lo] = data[q];
+            }
+        }
+        if (!unsorted) {
+            for (int64_t t = lane; t < len; t += 32) {
+                ind_out[o + t] = (int32_t)indices[lo + t];
+                dat_out[o + t] = (T)data[lo + t];
+            }
+            continue;
+        }
+        if (!short_row) continue;  // written by csr_prep_long_kernel from the sorted rows
+        __syncwarp();
+        for (int e = lane; e < (int)len; e += 32) {
+            const int32_t key = skey[wib][e];
+            bool first = true;
+            for (int e2 = 0; e2 < e; ++e2) first &= skey[wib][e2] != key;
+            sfirst[wib][e] = first;
+        }
+        __syncwarp();
+        for (int e = lane; e < (int)len; e += 32) {
+            if (!sfirst[wib][e]) continue;
+            const int32_t key = skey[wib][e];
+            int rank = 0;  // distinct columns below this one
+            for (int e2 = 0; e2 < (int)len; ++e2) rank += sfirst[wib][e2] && skey[wib][e2] < key;
+            double sum = sval[wib][e];  // from the first occurrence, in original order
+            for (int e2 = e + 1; e2 < (int)len; ++e2)
+                if (skey[wib][e2] == key) sum += sval[wib][e2];
+            ind_out[o + rank] = key;
+            dat_out[o + rank] = (T)sum;
+        }
+        __syncwarp();  // shared rows are rewritten by the next row
+    }
+}
+
+// Gathers the narrowed columns of the long unsorted rows into one buffer
+// (segment j = long row j) with each entry's position within its row.
+__global__ void __launch_bounds__(256)
+    csr_prep_gather_long_kernel(const int64_t* __restrict__ indptr,
+                                const int64_t* __restrict__ long_row, int64_t n_long,
+                                const int64_t* __restrict__ seg_lo,
+                                const int32_t* __restrict__ ind_narrow, uint32_t* __restrict__ key,
+                                uint32_t* __restrict__ pos) {
+    for (int64_t j = blockIdx.x; j < n_long; j += gridDim.x) {
+        const int64_t lo = indptr[long_row[j]], s0 = seg_lo[j], len = seg_lo[j + 1] - s0;
+        for (int64_t t = threadIdx.x; t < len; t += blockDim.x) {
+            key[s0 + t] = (uint32_t)ind_narrow[lo + t];
+            pos[s0 + t] = (uint32_t)t;
+        }
+    }
+}
+
+// Counts (write = false) or writes (write = true) the distinct columns of the
+// sorted long rows: warp per row; a column's first sorted entry sums the run
+// of its duplicates in original order (the sort is stable).
+template <class T, bool WRITE>
+__global__ void __launch_bounds__(kPrepWarps * 32)
+    csr_prep_long_kernel(const int64_t* __restrict__ indptr, const double* __restrict__ data,
+                         const int64_t* __restrict__ long_row, int64_t n_long,
+                         const int64_t* __restrict__ seg_lo, const uint32_t* __restrict__ key,
+                         const uint32_t* __restrict__ pos, int64_t* __restrict__ cnt_or_ptr,
+                         int32_t* __restrict__ ind_out, T* __restrict__ dat_out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
+    for (int64_t j = (int64_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5); j < n_long;
+         j += nwarps) {
+        const int64_t r = long_row[j], lo = indptr[r];
+        const int64_t s0 = seg_lo[j], s1 = seg_lo[j + 1];
+        int64_t o = WRITE ? cnt_or_ptr[r] : 0;
+        int64_t heads = 0;
+        for (int64_t base = s0; base < s1; base += 32) {
+            const int64_t p = base + lane;
+            const bool in = p < s1;
+            const uint32_t kk = in ? key[p] : 0u;
+            const bool head = in && (p == s0 || key[p - 1] != kk);
+            const unsigned mask = __ballot_sync(0xffffffffu, head);
+            if (WRITE && head) {
+                double sum = data[lo + pos[p]];  // from the first occurrence
+                for (int64_t p2 = p + 1; p2 < s1 && key[p2] == kk; ++p2) sum += data[lo + pos[p2]];
+                const int64_t at = o + __popc(mask & ((1u << lane) - 1u));
+                ind_out[at] = (int32_t)kk;
+                dat_out[at] = (T)sum;
+            }
+            o += __popc(mask);
+            heads += __popc(mask);
+        }
+        if (!WRITE && lane == 0) cnt_or_ptr[r] = heads;
+    }
+}
+
+int key_bits_for(int64_t n_features) {
+    int b = 1;
+    while (b < 31 && (int64_t(1) << b) < n_features) ++b;
+    return b;
+}
+
+template <class T>
+int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features, int64_t nnz,
+                 const int64_t* indptr, const int64_t* indices, const double* data,
+                 int64_t* indptr_out, int32_t* ind_out, T* dat_out) {
+    if (n_rows == 0) {
+        int64_t first = -1;
+        d2h(&first, indptr, 1, s, "CSR prep indptr");
+        MFM_CUDA(cudaStreamSynchronize(s), "CSR prep indptr");
+        if (first != 0 || nnz != 0) fail(MFM_ERR_INVALID, "indptr must start at 0 and end at nnz");
+        MFM_CUDA(cudaMemcpyAsync(indptr_out, indptr, sizeof(int64_t), cudaMemcpyDeviceToDevice, s),
+                 "CSR prep indptr");
+        MFM_CUDA(cudaStreamSynchronize(s), "CSR prep");
+        return 0;
+    }
+    // flags (2 words) + the long-row list; counts go straight into indptr_out
+    const int64_t max_long = std::min<int64_t>(n_rows, nnz / (kShortRow + 1) + 1);
+    DevBuf<unsigned> flags(device, 2);
+    DevBuf<int64_t> long_row(device, (size_t)max_long);
+    MFM_CUDA(cudaMemsetAsync(flags.ptr, 0, 2 * sizeof(unsigned), s), "memset");
+    const unsigned grid = warp_grid(device, n_rows, kPrepWarps, 8);
+    csr_prep_count_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(
+        indptr, indices, data, n_rows, nnz, n_features, ind_out, dat_out, indptr_out,
+        long_row.ptr, max_long, flags.ptr);
+    MFM_CHECK_LAUNCH("CSR prep count");
+    unsigned h[2] = {0, 0};
+    d2h(h, flags.ptr, 2, s, "CSR prep flags");
+    MFM_CUDA(cudaStreamSynchronize(s), "CSR prep count");
+    if (h[0] & kBadOrder) fail(MFM_ERR_INVALID, "indptr must be non-decreasing");
+    if (h[0] & kBadEnds) fail(MFM_ERR_INVALID, "indptr must start at 0 and end at nnz");
+    if (h[0] & kBadIndex)
+        fail(MFM_ERR_INVALID, fmt("column index out of range [0, %lld)", (long long)n_features));
+    if (!(h[0] & kUnsorted)) {  // canonical already: the narrowed copy is the result
+        MFM_CUDA(cudaMemcpyAsync(indptr_out, indptr, (n_rows + 1) * sizeof(int64_t),
+                                 cudaMemcpyDeviceToDevice, s),
+                 "CSR prep indptr");
+        MFM_CUDA(cudaStreamSynchronize(s), "CSR prep");
+        return nnz;
+    }
+
+    // long unsorted rows: stable segmented sort of their columns
+    const int64_t n_long = h[1];  // <= max_long once the CSR is valid
+    if (n_long > max_long) fail(MFM_ERR_INVALID, "indptr must be non-decreasing");
+    DevBuf<int64_t> seg_lo;
+    DevBuf<uint32_t> k0, v0, k1, v1;
+    SortResult sorted{nullptr, nullptr};
+    if (n_long > 0) {
+        std::vector<int64_t> rows(n_long), bounds(n_rows + 1), lo(n_long + 1, 0);
+        d2h(rows.data(), long_row.ptr, n_long, s, "CSR prep long rows");
+        d2h(bounds.data(), indptr, n_rows + 1, s, "CSR prep indptr");
+        MFM_CUDA(cudaStreamSynchronize(s), "CSR prep long rows");
+        std::sort(rows.begin(), rows.end());  // a fixed buffer layout
+        for (int64_t j = 0; j < n_long; ++j)
+            lo[j + 1] = lo[j] + (bounds[rows[j] + 1] - bounds[rows[j]]);
+        const int64_t total = lo[n_long];
+        h2d(long_row.ptr, rows.data(), n_long, s, "CSR prep long rows");
+        seg_lo.alloc(device, n_long + 1);
+        h2d(seg_lo.ptr, lo.data(), n_long + 1, s, "CSR prep segments");
+        k0.alloc(device, total);
+        v0.alloc(device, total);
+        k1.alloc(device, total);
+        v1.alloc(device, total);
+        csr_prep_gather_long_kernel<<<(unsigned)std::min<int64_t>(n_long, 65535), 256, 0, s>>>(
+            indptr, long_row.ptr, n_long, seg_lo.ptr, ind_out, k0.ptr, v0.ptr);
+        MFM_CHECK_LAUNCH("CSR prep gather");
+        sorted = segmented_sort(device, s, k0.ptr, v0.ptr, k1.ptr, v1.ptr, seg_lo.ptr, n_long,
+                                total, key_bits_for(n_features));
+        const unsigned lg = warp_grid(device, n_long, kPrepWarps, 8);
+        csr_prep_long_kernel<T, false><<<lg, kPrepWarps * 32, 0, s>>>(
+            indptr, data, long_row.ptr, n_long, seg_lo.ptr, sorted.keys, sorted.vals, indptr_out,
+            nullptr, nullptr);
+        MFM_CHECK_LAUNCH("CSR prep long count");
+    }
+    exclusive_scan<int64_t, int64_t>(device, s, indptr_out, n_rows, indptr_out);
+    csr_prep_write_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(indptr, indices, data, n_rows,
+                                                              indptr_out, ind_out, dat_out);
+    MFM_CHECK_LAUNCH("CSR prep write");
+    if (n_long > 0) {
+        const unsigned lg = warp_grid(device, n_long, kPrepWarps, 8);
+        csr_prep_long_kernel<T, true><<<lg, kPrepWarps * 32, 0, s>>>(
+            indptr, data, long_row.ptr, n_long, seg_lo.ptr, sorted.keys, sorted.vals, indptr_out,
+            ind_out, dat_out);
+        MFM_CHECK_LAUNCH("CSR prep long write");
+    }
+    int64_t nnz_out = 0;
+    d2h(&nnz_out, indptr_out + n_rows, 1, s, "CSR prep nnz");
+    MFM_CUDA(cudaStreamSynchronize(s), "CSR prep");
+    return nnz_out;
+}
+
+}  // namespace
+}  // namespace mfm
+
+using namespace mfm;
+
+extern "C" int mfm_csr_prep_device(int dtype, int device, int64_t n_rows, int64_t n_features,
+                                   int64_t nnz, const int64_t* indptr, const int64_t* indices,
+                                   const double* data, int64_t* indptr_out, int32_t* indices_out,
+                                   void* data_out, int64_t* nnz_out, void* stream) {
+    return guarded([&] {
+        if (n_rows < 0 || nnz < 0 || n_features < 0) fail(MFM_ERR_INVALID, "negative CSR size");
+        if (!indptr || !indptr_out || !nnz_out)
+            fail(MFM_ERR_INVALID, "indptr, indptr_out and nnz_out must be provided");
+        if (nnz > 0 && (!indices || !data || !indices_out || !data_out))
+            fail(MFM_ERR_INVALID, "indices and data (in and out) must be provided when nnz > 0");
+        if (n_features > INT32_MAX)
+            fail(MFM_ERR_UNSUPPORTED, fmt("n_features %lld exceeds the engine's 2^31-1 limit",
+                                          (long long)n_features));
+        if (dtype != MFM_DTYPE_F32 && dtype != MFM_DTYPE_F64)
+            fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
+        DeviceGuard g(device);
+        cudaStream_t s = (cudaStream_t)stream;
+        *nnz_out = dtype == MFM_DTYPE_F32
+                       ? csr_prep<float>(device, s, n_rows, n_features, nnz, indptr, indices,
+                                         data, indptr_out, indices_out, (float*)data_out)
+                       : csr_prep<double>(device, s, n_rows, n_features, nnz, indptr, indices,
+                                          data, indptr_out, indices_out, (double*)data_out);
+    });
+}

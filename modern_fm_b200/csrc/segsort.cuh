@@ -28,7 +28,7 @@ constexpr int kSortNT = 256;    // threads per tile (= digits per pass)
 constexpr int kSortItems = 16;  // keys per thread
 constexpr int kSortTile = kSortNT * kSortItems;
 
-__global__ void __launch_bounds__(256)
+static __global__ void __launch_bounds__(256)
     seg_hist_kernel(const uint32_t* __restrict__ keys, const int64_t* __restrict__ tile_lo,
                     const int64_t* __restrict__ tile_hi, int shift,
                     uint32_t* __restrict__ hist) {
@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(256)
 
 // One block (256 threads, thread = digit) per segment; converts the tiles'
 // counts into absolute output offsets in place.
-__global__ void __launch_bounds__(256)
+static __global__ void __launch_bounds__(256)
     seg_offsets_kernel(const int64_t* __restrict__ seg_lo, const int64_t* __restrict__ seg_tile,
                        uint32_t* __restrict__ hist) {
     __shared__ uint32_t sm[8];
@@ -192,7 +192,7 @@ __global__ void __launch_bounds__(kSortNT)
 
 // Builds the tile table: segment b = [seg_lo[b], seg_lo[b+1]) gets
 // ceil(len/kSortTile) tiles numbered from seg_tile[b].
-__global__ void seg_tiles_kernel(const int64_t* __restrict__ seg_lo, int64_t n_seg,
+static __global__ void seg_tiles_kernel(const int64_t* __restrict__ seg_lo, int64_t n_seg,
                                  const int64_t* __restrict__ seg_tile,
                                  int64_t* __restrict__ tile_lo, int64_t* __restrict__ tile_hi,
                                  int64_t* __restrict__ tile_seg_lo) {
@@ -207,7 +207,7 @@ __global__ void seg_tiles_kernel(const int64_t* __restrict__ seg_lo, int64_t n_s
     }
 }
 
-__global__ void seg_tile_count_kernel(const int64_t* __restrict__ seg_lo, int64_t n_seg,
+static __global__ void seg_tile_count_kernel(const int64_t* __restrict__ seg_lo, int64_t n_seg,
                                       int64_t* __restrict__ cnt) {
     const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (b < n_seg) cnt[b] = ceil_div(seg_lo[b + 1] - seg_lo[b], kSortTile);

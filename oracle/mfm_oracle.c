@@ -69,6 +69,50 @@ int orc_check_field_ids(const int64_t* field_ids, int64_t len, int64_t n_feature
     return 0;
 }
 
+/* _prep_csr — python/modern_fm/_backend.py:44-52: `X.astype(np.float64);
+ * X.sum_duplicates()`. scipy sorts each row by column and then adds each
+ * column's duplicates left to right (explicit zeros are kept). Restated with a
+ * stable sort, so a column's duplicates are added in their original order; the
+ * result equals scipy's whenever scipy's order of equal columns is that order
+ * (rows it does not reorder, at most two duplicates of a column) and differs
+ * from it by rounding otherwise. The input must pass orc_check_csr. Writes
+ * indptr_out (n_rows+1), indices_out / data_out (up to nnz); returns the
+ * canonical entry count. */
+int64_t orc_prep_csr(int64_t n_rows, const int64_t* indptr, const int64_t* indices,
+                     const double* data, int64_t* indptr_out, int64_t* indices_out,
+                     double* data_out) {
+    int64_t o = 0, cap = 0;
+    int64_t* perm = NULL;
+    indptr_out[0] = 0;
+    for (int64_t r = 0; r < n_rows; ++r) {
+        const int64_t lo = indptr[r], len = indptr[r + 1] - lo;
+        if (len > cap) {
+            cap = len;
+            perm = (int64_t*)realloc(perm, (size_t)cap * sizeof(int64_t));
+        }
+        /* stable insertion sort of the row's positions by column */
+        for (int64_t t = 0; t < len; ++t) {
+            int64_t u = t;
+            while (u > 0 && indices[lo + perm[u - 1]] > indices[lo + t]) {
+                perm[u] = perm[u - 1];
+                --u;
+            }
+            perm[u] = t;
+        }
+        for (int64_t t = 0; t < len;) {
+            const int64_t col = indices[lo + perm[t]];
+            double x = data[lo + perm[t]];
+            for (++t; t < len && indices[lo + perm[t]] == col; ++t) x += data[lo + perm[t]];
+            indices_out[o] = col;
+            data_out[o] = x;
+            ++o;
+        }
+        indptr_out[r + 1] = o;
+    }
+    free(perm);
+    return o;
+}
+
 /* ------------------------------------------------------------------------ */
 /* optimizer primitives — rust/src/optimizer.rs                             */
 /* ------------------------------------------------------------------------ */

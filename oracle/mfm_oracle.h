@@ -58,6 +58,11 @@ int orc_check_csr(const int64_t* indptr, int64_t indptr_len, const int64_t* indi
                   int errlen);
 int orc_check_field_ids(const int64_t* field_ids, int64_t len, int64_t n_features,
                         int64_t n_fields, char* err, int errlen);
+/* _prep_csr (python/modern_fm/_backend.py:44-52): sort each row by column and
+ * sum duplicate columns, stable order. Returns the canonical entry count. */
+int64_t orc_prep_csr(int64_t n_rows, const int64_t* indptr, const int64_t* indices,
+                     const double* data, int64_t* indptr_out, int64_t* indices_out,
+                     double* data_out);
 
 /* ---- prediction (serial per row in the reference; n_threads splits rows) ---- */
 void orc_fm_predict_csr(const int64_t* indptr, const int64_t* indices, const double* data,

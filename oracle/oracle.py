@@ -66,6 +66,8 @@ def lib():
         L.orc_check_field_ids.restype = ct.c_int
         L.orc_check_field_ids.argtypes = [_i64p, ct.c_int64, ct.c_int64, ct.c_int64,
                                           ct.c_char_p, ct.c_int]
+        L.orc_prep_csr.restype = ct.c_int64
+        L.orc_prep_csr.argtypes = [ct.c_int64, _i64p, _i64p, _f64p, _i64p, _i64p, _f64p]
         L.orc_sigmoid.restype = ct.c_double
         L.orc_sigmoid.argtypes = [ct.c_double]
         for name in ("orc_fm_fit_csr", "orc_ffm_fit_csr", "orc_fwfm_fit_csr",
@@ -106,6 +108,25 @@ def _check_field_ids(field_ids, n_features, n_fields):
 
 def _nthreads(n_threads):
     return max(1, int(n_threads))
+
+
+# --------------------------------------------------------------------------
+# CSR canonicalisation (python/modern_fm/_backend.py:44-52)
+# --------------------------------------------------------------------------
+
+def prep_csr(indptr, indices, data, n_features):
+    """`_prep_csr` restated: validate, sort each row by column and sum
+    duplicate columns in float64 in their original order. Returns
+    (indptr, indices, data) as int64 / int64 / float64 arrays."""
+    indptr, indices, data = _i64(indptr), _i64(indices), _f64(data)
+    _check_csr(indptr, indices, data, n_features)
+    n_rows = len(indptr) - 1
+    ip = np.empty(n_rows + 1, dtype=np.int64)
+    ix = np.empty(max(len(indices), 1), dtype=np.int64)
+    dv = np.empty(max(len(indices), 1))
+    m = lib().orc_prep_csr(n_rows, _p(indptr, _i64p), _p(indices, _i64p), _p(data),
+                           _p(ip, _i64p), _p(ix, _i64p), _p(dv))
+    return ip, ix[:m].copy(), dv[:m].copy()
 
 
 # --------------------------------------------------------------------------
