@@ -207,6 +207,21 @@ int mfm_csr_prep_device(int dtype, int device, int64_t n_rows, int64_t n_feature
                         int64_t* indptr_out, int32_t* indices_out, void* data_out,
                         int64_t* nnz_out, void* stream);
 
+/* ---- early-stopping evaluation on the device -----------------------------
+ * Replaces the host evaluation the reference's early-stopped FM fits run after
+ * every epoch, `metric(y_val, fm_predict_fast(X_val, w0, w, V))`
+ * (python/modern_fm/fm.py:321-322) with logistic_loss (label smoothing
+ * applied to the target) or squared_loss (python/modern_fm/losses.py:25-42,
+ * 64-68). The validation CSR and the parameters are DEVICE arrays in the
+ * compute layout of mfm_fm_predict_device; y and sample_weight are float64
+ * DEVICE arrays (sample_weight NULL = unweighted mean). The loss is reduced in
+ * float64 on the device in a fixed order (bitwise reproducible) and written to
+ * *loss_out (host); n_rows = 0 gives NaN, as NumPy's mean of nothing. */
+int mfm_fm_eval_device(int dtype, int device, const int64_t* indptr, const int32_t* indices,
+                       const void* data, int64_t n_rows, double w0, const void* w, const void* v,
+                       int64_t k, const double* y, const double* sample_weight, int loss,
+                       double label_smoothing, double* loss_out, void* stream);
+
 /* ---- allocation-free FM scoring --------------------------------------------
  * No counterpart in the reference: an addition for callers that cannot let
  * the library allocate GPU memory, such as a host that owns the whole device

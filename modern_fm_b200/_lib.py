@@ -94,6 +94,10 @@ _SIGNATURES = {
     "mfm_csr_prep_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_int64, ct.c_int64, ct.c_int64,
                                        ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p,
                                        ct.c_void_p, ct.c_void_p, i64p, ct.c_void_p]),
+    "mfm_fm_eval_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p, ct.c_void_p,
+                                      ct.c_int64, ct.c_double, ct.c_void_p, ct.c_void_p,
+                                      ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_double,
+                                      f64p, ct.c_void_p]),
     "mfm_fm_predict_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_double, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]),

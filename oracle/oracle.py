@@ -130,6 +130,35 @@ def prep_csr(indptr, indices, data, n_features):
 
 
 # --------------------------------------------------------------------------
+# validation metrics (python/modern_fm/losses.py)
+# --------------------------------------------------------------------------
+
+def _weighted_mean(values, sample_weight):
+    """losses.py:25-28."""
+    if sample_weight is None:
+        return values.mean()
+    sample_weight = np.asarray(sample_weight, dtype=np.float64)
+    return (values * sample_weight).sum() / sample_weight.sum()
+
+
+def logistic_loss(y, raw, label_smoothing=0.0, sample_weight=None):
+    """losses.py:31-42: max(s, 0) - s*y + log1p(exp(-|s|)), smoothed target."""
+    y = np.asarray(y, dtype=np.float64)
+    s = np.asarray(raw, dtype=np.float64)
+    if label_smoothing:
+        y = y * (1.0 - label_smoothing) + 0.5 * label_smoothing
+    return _weighted_mean(np.maximum(s, 0.0) - s * y + np.log1p(np.exp(-np.abs(s))),
+                          sample_weight)
+
+
+def squared_loss(y, raw, sample_weight=None):
+    """losses.py:64-68: 0.5 (s - y)^2."""
+    y = np.asarray(y, dtype=np.float64)
+    s = np.asarray(raw, dtype=np.float64)
+    return _weighted_mean(0.5 * (s - y) ** 2, sample_weight)
+
+
+# --------------------------------------------------------------------------
 # prediction
 # --------------------------------------------------------------------------
 
