@@ -16,14 +16,17 @@
 //   * narrows to int32 columns and values in the compute dtype, so the result
 //     feeds mfm_{fm,ffm,fwfm}_predict_device and mfm_fm_fit_device directly.
 //
-// Work split (warp per row, rows grid-strided):
-//   1. csr_prep_count_kernel: one pass over the input; checks, narrows every
-//      entry in place of the output (the final result when the matrix is
-//      already canonical, the common case: nothing else runs then) and writes
-//      each row's distinct-column count. Rows of up to kShortRow entries that
-//      are out of order are counted in shared memory (first occurrences of
-//      each column); longer ones are listed for the sort.
-//   2. exclusive scan of the counts -> the output indptr.
+// Work split:
+//   1. one streaming pass: csr_prep_rows_kernel (thread per row: indptr checks,
+//      a bit per row start, the output indptr) and csr_prep_flat_kernel (four
+//      coalesced entries per thread: range check, "greater than the previous
+//      entry unless it starts a row", the narrowed copy). When every row is in
+//      order, the common case, that copy is the result and nothing else runs.
+//   2. otherwise csr_prep_count_kernel (warp per row, rows grid-strided)
+//      writes each row's distinct-column count: rows of up to kShortRow entries
+//      that are out of order are counted in shared memory (first occurrences of
+//      each column); longer ones are listed for the sort. An exclusive scan of
+//      the counts gives the output indptr.
 //   3. long unsorted rows only: their narrowed columns are gathered into one
 //      buffer and sorted stably within each row by the segmented radix sort
 //      (segsort.cuh), so equal columns keep their original order.
@@ -50,6 +53,75 @@ enum : unsigned {
     kBadIndex = 4u,   // a column index outside [0, n_features)
     kUnsorted = 8u,   // some row is out of order or holds duplicates
 };
+
+// Pass 1, row part: one thread per row. Validates the row's bounds, marks
+// each nonempty row's first entry in `starts` (one bit per entry) and writes
+// the output indptr as a copy of the input's (final when every row turns out
+// to be in order; rewritten by the scan otherwise).
+__global__ void __launch_bounds__(256)
+    csr_prep_rows_kernel(const int64_t* __restrict__ indptr, int64_t n_rows, int64_t nnz,
+                         int64_t* __restrict__ indptr_out, unsigned* __restrict__ starts,
+                         unsigned* flags) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    unsigned bad = 0;
+    if (r < n_rows) {
+        const int64_t lo = indptr[r], hi = indptr[r + 1];
+        if (hi < lo)
+            bad = kBadOrder;
+        else if (lo < 0 || hi > nnz || (r == 0 && lo != 0) || (r == n_rows - 1 && hi != nnz))
+            bad = kBadEnds;
+        else if (lo < hi)
+            atomicOr(starts + (lo >> 5), 1u << (lo & 31));
+        indptr_out[r + 1] = hi;
+        if (r == 0) indptr_out[0] = lo;
+    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if (bad && (threadIdx.x & 31) == 0) atomicOr(flags, bad);
+}
+
+// Pass 1, entry part: kFlatItems entries per thread, strided by the block
+// (entry q = tile + i * kFlatNT + tid) so every load and store is coalesced
+// and a warp's 32 entries share one word of `starts`. Checks each column's
+// range and that it exceeds its predecessor unless it starts a row, and writes
+// the narrowed entry at the same position of the output.
+constexpr int kFlatNT = 256, kFlatItems = 4;
+template <class T>
+__global__ void __launch_bounds__(kFlatNT)
+    csr_prep_flat_kernel(const int64_t* __restrict__ indices, const double* __restrict__ data,
+                         int64_t nnz, int64_t n_features, const unsigned* __restrict__ starts,
+                         int32_t* __restrict__ ind_out, T* __restrict__ dat_out,
+                         unsigned* flags) {
+    const int64_t tile = (int64_t)blockIdx.x * (kFlatNT * kFlatItems);
+    const int lane = threadIdx.x & 31;
+    int64_t c[kFlatItems], pv[kFlatItems];
+    double v[kFlatItems];
+    unsigned sw[kFlatItems];
+#pragma unroll
+    for (int i = 0; i < kFlatItems; ++i) {  // every load issued before any use
+        const int64_t q = tile + i * kFlatNT + threadIdx.x;
+        const bool in = q < nnz;
+        c[i] = in ? indices[q] : 0;
+        v[i] = in ? data[q] : 0.0;
+        pv[i] = (lane == 0 && in && q > 0) ? indices[q - 1] : 0;  // outside the warp's chunk
+        sw[i] = in ? starts[q >> 5] : 0u;
+    }
+    unsigned bad = 0;
+#pragma unroll
+    for (int i = 0; i < kFlatItems; ++i) {
+        const int64_t q = tile + i * kFlatNT + threadIdx.x;
+        int64_t prev = __shfl_up_sync(0xffffffffu, c[i], 1);
+        if (lane == 0) prev = pv[i];
+        if (q < nnz) {
+            const bool start = (sw[i] >> (q & 31)) & 1u;
+            if (c[i] < 0 || c[i] >= n_features) bad |= kBadIndex;
+            if (!start && !(c[i] > prev)) bad |= kUnsorted;
+            ind_out[q] = (int32_t)c[i];
+            dat_out[q] = (T)v[i];
+        }
+    }
+    bad = __reduce_or_sync(0xffffffffu, bad);
+    if (bad && lane == 0) atomicOr(flags, bad);
+}
 
 // flags[0]: kBad* / kUnsorted bits; flags[1]: number of long unsorted rows.
 template <class T>
@@ -269,9 +341,28 @@ int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features,
         MFM_CUDA(cudaStreamSynchronize(s), "CSR prep");
         return 0;
     }
-    // flags (2 words) + the long-row list; counts go straight into indptr_out
+    // pass 1 (streaming): validation, order check and the narrowed copy
+    DevBuf<unsigned> flags(device, 2), starts(device, (size_t)(nnz / 32 + 1));
+    MFM_CUDA(cudaMemsetAsync(flags.ptr, 0, 2 * sizeof(unsigned), s), "memset");
+    MFM_CUDA(cudaMemsetAsync(starts.ptr, 0, starts.bytes(), s), "memset");
+    csr_prep_rows_kernel<<<(unsigned)ceil_div(n_rows, 256), 256, 0, s>>>(
+        indptr, n_rows, nnz, indptr_out, starts.ptr, flags.ptr);
+    if (nnz > 0)
+        csr_prep_flat_kernel<T><<<(unsigned)ceil_div(nnz, kFlatNT * kFlatItems), kFlatNT, 0, s>>>(
+            indices, data, nnz, n_features, starts.ptr, ind_out, dat_out, flags.ptr);
+    MFM_CHECK_LAUNCH("CSR prep check");
+    unsigned h[2] = {0, 0};
+    d2h(h, flags.ptr, 2, s, "CSR prep flags");
+    MFM_CUDA(cudaStreamSynchronize(s), "CSR prep check");
+    if (h[0] & kBadOrder) fail(MFM_ERR_INVALID, "indptr must be non-decreasing");
+    if (h[0] & kBadEnds) fail(MFM_ERR_INVALID, "indptr must start at 0 and end at nnz");
+    if (h[0] & kBadIndex)
+        fail(MFM_ERR_INVALID, fmt("column index out of range [0, %lld)", (long long)n_features));
+    if (!(h[0] & kUnsorted)) return nnz;  // canonical already: pass 1 wrote the result
+
+    // some row is out of order: per-row distinct counts (and the long-row
+    // list); counts go straight into indptr_out
     const int64_t max_long = std::min<int64_t>(n_rows, nnz / (kShortRow + 1) + 1);
-    DevBuf<unsigned> flags(device, 2);
     DevBuf<int64_t> long_row(device, (size_t)max_long);
     MFM_CUDA(cudaMemsetAsync(flags.ptr, 0, 2 * sizeof(unsigned), s), "memset");
     const unsigned grid = warp_grid(device, n_rows, kPrepWarps, 8);
@@ -279,20 +370,8 @@ int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features,
         indptr, indices, data, n_rows, nnz, n_features, ind_out, dat_out, indptr_out,
         long_row.ptr, max_long, flags.ptr);
     MFM_CHECK_LAUNCH("CSR prep count");
-    unsigned h[2] = {0, 0};
     d2h(h, flags.ptr, 2, s, "CSR prep flags");
     MFM_CUDA(cudaStreamSynchronize(s), "CSR prep count");
-    if (h[0] & kBadOrder) fail(MFM_ERR_INVALID, "indptr must be non-decreasing");
-    if (h[0] & kBadEnds) fail(MFM_ERR_INVALID, "indptr must start at 0 and end at nnz");
-    if (h[0] & kBadIndex)
-        fail(MFM_ERR_INVALID, fmt("column index out of range [0, %lld)", (long long)n_features));
-    if (!(h[0] & kUnsorted)) {  // canonical already: the narrowed copy is the result
-        MFM_CUDA(cudaMemcpyAsync(indptr_out, indptr, (n_rows + 1) * sizeof(int64_t),
-                                 cudaMemcpyDeviceToDevice, s),
-                 "CSR prep indptr");
-        MFM_CUDA(cudaStreamSynchronize(s), "CSR prep");
-        return nnz;
-    }
 
     // long unsorted rows: stable segmented sort of their columns
     const int64_t n_long = h[1];  // <= max_long once the CSR is valid

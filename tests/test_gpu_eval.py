@@ -20,9 +20,9 @@ pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
 
-def _case(seed, n=5000, d=3000, k=16):
+def _case(seed, n=5000, d=3000, k=16, density=0.01):
     rng = np.random.default_rng(seed)
-    X = sp.random(n, d, density=0.01, format="csr", random_state=seed,
+    X = sp.random(n, d, density=density, format="csr", random_state=seed,
                   data_rvs=lambda m: rng.lognormal(0.0, 1.0, size=m))
     ip, ix, dv = X.indptr.astype(np.int64), X.indices.astype(np.int64), X.data
     w0, w, V = -0.2, rng.normal(size=d) * 0.3, rng.normal(size=(d, k)) * 0.2
@@ -64,7 +64,7 @@ def test_eval_matches_oracle(dtype, rtol, loss, eps, weighted):
 
 
 def test_eval_is_bitwise_reproducible():
-    case = _case(2, n=200_000, d=20_000)
+    case = _case(2, n=200_000, d=20_000, density=0.0005)
     a = _run(case, "float64", "logistic", 0.0, True)
     b = _run(case, "float64", "logistic", 0.0, True)
     assert a == b and math.isfinite(a)
