@@ -1,10 +1,11 @@
 """Generate the golden fixtures in tests/golden/ from the reference's NumPy
 ground truth (modern_fm v1.1.1, python/modern_fm/_reference.py and
-_reference_train.py).
+_reference_train.py), its CSR preparation (_backend._prep_csr) and its
+validation metrics (losses.py).
 
 Run in a container where the reference source tree is present:
 
-    python tests/golden/make_golden.py --reference /path/to/reference/python
+    python tests/golden/make_golden.py --reference /path/to/reference/python [--only prep losses]
 
 The reference specifies these NumPy trainers as bit-for-bit with its Rust CPU
 engine at n_jobs=1 (_reference_train.py:8-18), so the fixtures pin both the C
@@ -221,18 +222,110 @@ def make_train_multiclass(T):
     w.save("train_multiclass.npz")
 
 
+def _raw_csr(rng, n_rows, n_features, lens, dup_pool=None, sort_rows=False):
+    """Rows of the given lengths; columns drawn with repeats from `dup_pool`
+    columns per row (None: any column), in draw order unless sorted; values
+    N(0, 1) with some explicit zeros and negative zeros."""
+    ip, ix, dv = [0], [], []
+    for r in range(n_rows):
+        L = int(lens[r % len(lens)])
+        if dup_pool is None:
+            c = rng.integers(0, n_features, size=L)
+        else:
+            base = rng.choice(n_features, size=min(dup_pool, n_features), replace=False)
+            c = base[rng.integers(0, len(base), size=L)]
+        if sort_rows:
+            c = np.sort(c, kind="stable")
+        v = rng.normal(size=L)
+        v[rng.random(L) < 0.05] = 0.0
+        v[rng.random(L) < 0.02] = -0.0
+        ix.extend(c.tolist())
+        dv.extend(v.tolist())
+        ip.append(len(ix))
+    return (np.array(ip, dtype=np.int64), np.array(ix, dtype=np.int64),
+            np.array(dv, dtype=np.float64))
+
+
+def make_prep(B):
+    """The reference's `_prep_csr` (python/modern_fm/_backend.py:44-52) on raw
+    CSR inputs. `exact` marks cases where the duplicate-summation order is
+    the original one (canonical input, rows already in order, at most two
+    duplicates of a column), so the values are pinned bitwise."""
+    w = Writer()
+    rng = np.random.default_rng(7)
+    cases = [
+        ("canonical", dict(n_rows=200, n_features=300, lens=[0, 3, 12, 40]), True),
+        ("sorted_dups", dict(n_rows=100, n_features=64, lens=[0, 1, 5, 39, 300], dup_pool=8,
+                             sort_rows=True), True),
+        ("unsorted_pairs", dict(n_rows=80, n_features=1 << 22, lens=[2, 17, 39, 400]), True),
+        ("unsorted_short_many", dict(n_rows=400, n_features=40, lens=[0, 3, 9, 16], dup_pool=4),
+         False),
+        ("unsorted_long_many", dict(n_rows=16, n_features=5000,
+                                    lens=[257, 3, 300, 0, 1000, 39, 4096, 4097], dup_pool=40),
+         False),
+    ]
+    for name, kw, exact in cases:
+        ip, ix, dv = _raw_csr(rng, **kw)
+        if name == "canonical":  # strictly increasing rows, no duplicates
+            X = sp.csr_matrix((dv, ix, ip), shape=(len(ip) - 1, kw["n_features"]))
+            X.sum_duplicates()
+            ip, ix, dv = X.indptr.astype(np.int64), X.indices.astype(np.int64), X.data
+        X = sp.csr_matrix((dv.copy(), ix.copy(), ip.copy()), shape=(len(ip) - 1, kw["n_features"]))
+        oip, oix, odv, nf = B._prep_csr(X)
+        w.add(name, dict(n_features=int(nf), exact=exact), indptr=ip, indices=ix, data=dv,
+              out_indptr=oip, out_indices=oix, out_data=odv)
+    w.save("prep.npz")
+
+
+def make_losses(L):
+    """The reference's validation metrics (python/modern_fm/losses.py:25-68)
+    on seeded raw scores: logistic (with and without label smoothing and
+    sample weights) and squared."""
+    w = Writer()
+    rng = np.random.default_rng(8)
+    for i, (loss, eps, weighted) in enumerate([("logistic", 0.0, False), ("logistic", 0.1, True),
+                                               ("logistic", 0.0, True), ("squared", 0.0, False),
+                                               ("squared", 0.0, True)]):
+        n = 1000
+        raw = rng.normal(size=n) * 3.0
+        raw[:5] = [0.0, 40.0, -40.0, 700.0, -700.0]  # the stable form's edge cases
+        y = (rng.random(n) < 0.3).astype(np.float64) if loss == "logistic" else rng.normal(size=n)
+        sw = rng.uniform(0.5, 2.0, size=n)
+        if loss == "logistic":
+            val = L.logistic_loss(y, raw, label_smoothing=eps, sample_weight=sw if weighted else None)
+        else:
+            val = L.squared_loss(y, raw, sample_weight=sw if weighted else None)
+        w.add(f"{loss}_{i}", dict(loss=loss, label_smoothing=eps, weighted=weighted),
+              raw=raw, y=y, sample_weight=sw, value=np.array([val]))
+    w.save("losses.npz")
+
+
+MAKERS = ("predict", "train_binary", "train_multiclass", "prep", "losses")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference/python",
                     help="path to the reference's python/ directory")
+    ap.add_argument("--only", nargs="*", choices=MAKERS, default=list(MAKERS),
+                    help="fixture files to (re)generate")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
+    from modern_fm import _backend as B  # noqa: E402
     from modern_fm import _reference as R  # noqa: E402
     from modern_fm import _reference_train as T  # noqa: E402
+    from modern_fm import losses as L  # noqa: E402
 
-    make_predict(R)
-    make_train_binary(T)
-    make_train_multiclass(T)
+    if "predict" in args.only:
+        make_predict(R)
+    if "train_binary" in args.only:
+        make_train_binary(T)
+    if "train_multiclass" in args.only:
+        make_train_multiclass(T)
+    if "prep" in args.only:
+        make_prep(B)
+    if "losses" in args.only:
+        make_losses(L)
 
 
 if __name__ == "__main__":

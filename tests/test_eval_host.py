@@ -7,6 +7,7 @@ import math
 import numpy as np
 import pytest
 
+import golden_io
 from oracle import oracle as O
 
 
@@ -38,3 +39,16 @@ def test_device_eval_rejects_host_tensors():
     with pytest.raises(ValueError):
         fm_eval_device(z64, torch.zeros(1, dtype=torch.int32), torch.zeros(1), 0.0,
                        torch.zeros(3), torch.zeros(3, 2), torch.zeros(1, dtype=torch.float64))
+
+
+@pytest.mark.parametrize("case", golden_io.load("losses.npz"), ids=lambda c: c.name)
+def test_oracle_losses_match_reference_golden(case):
+    """Fixtures from the reference's own losses.py (tests/golden/make_golden.py):
+    the same NumPy expressions, so the values are equal bitwise."""
+    sw = case.a["sample_weight"] if case["weighted"] else None
+    if case["loss"] == "logistic":
+        got = O.logistic_loss(case.a["y"], case.a["raw"], label_smoothing=case["label_smoothing"],
+                              sample_weight=sw)
+    else:
+        got = O.squared_loss(case.a["y"], case.a["raw"], sample_weight=sw)
+    assert got == case.a["value"][0]

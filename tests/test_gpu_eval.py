@@ -13,6 +13,7 @@ import numpy as np
 import pytest
 import scipy.sparse as sp
 
+import golden_io
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -78,3 +79,18 @@ def test_eval_empty_and_invalid():
     assert math.isnan(_run(empty, "float64", "squared", 0.0, False))
     with pytest.raises(ValueError):
         _run(case, "float64", "hinge", 0.0, False)
+
+
+@pytest.mark.parametrize("case", golden_io.load("losses.npz"), ids=lambda c: c.name)
+@pytest.mark.parametrize("dtype,rtol", [("float64", 1e-12), ("float32", 1e-5)])
+def test_device_eval_matches_reference_golden(case, dtype, rtol):
+    """Against the reference's own losses.py values: one nonzero per row (its
+    own feature, value 1) with w = the fixture's raw scores, w0 = 0 and V = 0,
+    so each device score is the raw score (float64 exactly; float32 rounded
+    once)."""
+    raw = case.a["raw"]
+    n, k = len(raw), 4
+    c = (np.arange(n + 1, dtype=np.int64), np.arange(n, dtype=np.int64), np.ones(n), 0.0, raw,
+         np.zeros((n, k)), case.a["y"], case.a["sample_weight"])
+    got = _run(c, dtype, case["loss"], case["label_smoothing"], case["weighted"])
+    assert got == pytest.approx(case.a["value"][0], rel=rtol)

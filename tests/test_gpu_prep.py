@@ -10,6 +10,7 @@ float64 result rounded once to float32.
 import numpy as np
 import pytest
 
+import golden_io
 from oracle import oracle as O
 from test_prep_csr import raw_csr
 
@@ -137,3 +138,24 @@ def test_prepared_csr_scores_like_the_host_path():
     pp = O.prep_csr(ip, ix, dv, d)
     want = O.fm_predict_fast_csr(pp[0], pp[1], pp[2], d, w0, w, V)
     np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("case", golden_io.load("prep.npz"), ids=lambda c: c.name)
+def test_device_prep_matches_reference_golden(case):
+    """Against the reference's own `_prep_csr` output: structure exact; float64
+    values bitwise where the duplicates' order is defined (`exact`), 1e-14
+    otherwise; float32 values are those rounded once (one float32 ulp where
+    the float64 sums differ in their last bit)."""
+    ip, ix, dv, nf = case.a["indptr"], case.a["indices"], case.a["data"], case["n_features"]
+    want = case.a["out_data"]
+    for dtype in ("float64", "float32"):
+        a, b, c = _prep(ip, ix, dv, nf, dtype)
+        assert np.array_equal(a, case.a["out_indptr"])
+        assert np.array_equal(b.astype(np.int64), case.a["out_indices"])
+        ref = want if dtype == "float64" else want.astype(np.float32)
+        if case["exact"]:
+            assert np.array_equal(c.view(np.uint8), ref.view(np.uint8)), dtype
+        elif dtype == "float64":
+            np.testing.assert_allclose(c, ref, rtol=1e-14, atol=1e-14)
+        else:
+            np.testing.assert_allclose(c, ref, rtol=2.5e-7, atol=1e-12)

@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import scipy.sparse as sp
 
+import golden_io
 from oracle import oracle as O
 
 
@@ -132,3 +133,15 @@ def test_device_wrapper_rejects_host_tensors():
     with pytest.raises(ValueError):
         prep_csr_device(torch.zeros(2, dtype=torch.int64), torch.zeros(1, dtype=torch.int64),
                         torch.zeros(1, dtype=torch.float64), 4)
+
+
+@pytest.mark.parametrize("case", golden_io.load("prep.npz"), ids=lambda c: c.name)
+def test_oracle_matches_reference_prep_golden(case):
+    """Fixtures from the reference's own `_prep_csr` (tests/golden/make_golden.py)."""
+    got = O.prep_csr(case.a["indptr"], case.a["indices"], case.a["data"], case["n_features"])
+    assert np.array_equal(got[0], case.a["out_indptr"])
+    assert np.array_equal(got[1], case.a["out_indices"])
+    if case["exact"]:
+        assert np.array_equal(got[2].view(np.int64), case.a["out_data"].view(np.int64))
+    else:
+        np.testing.assert_allclose(got[2], case.a["out_data"], rtol=1e-14, atol=1e-14)
