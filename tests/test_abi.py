@@ -111,3 +111,39 @@ def test_exec_options_from_environment(monkeypatch):
     monkeypatch.setenv("MFM_B200_DTYPE", "float16")
     with pytest.raises(ValueError, match="unknown compute dtype"):
         _lib.exec_options()
+
+
+def _prep_call(dtype=_lib.MFM_DTYPE_F32, n_rows=2, n_features=4, nnz=2, null=False):
+    """mfm_csr_prep_device with dummy (never dereferenced) pointers: every case
+    below fails in the host checks, before any device work."""
+    p = None if null else 16
+    out = ct.c_int64(-1)
+    return _lib.lib().mfm_csr_prep_device(dtype, 0, n_rows, n_features, nnz, p, p, p, p, p, p,
+                                          ct.byref(out), None)
+
+
+@pytest.mark.parametrize("kw,code,msg", [
+    (dict(n_rows=-1), _lib.MFM_ERR_INVALID, "negative CSR size"),
+    (dict(nnz=-3), _lib.MFM_ERR_INVALID, "negative CSR size"),
+    (dict(null=True), _lib.MFM_ERR_INVALID, "must be provided"),
+    (dict(n_features=2**31), _lib.MFM_ERR_UNSUPPORTED, "2^31-1 limit"),
+    (dict(dtype=9), _lib.MFM_ERR_INVALID, "unknown dtype 9"),
+])
+def test_csr_prep_host_checks(kw, code, msg):
+    assert _prep_call(**kw) == code
+    assert msg in _lib.last_error()
+
+
+def test_eval_host_checks_and_empty_input():
+    L = _lib.lib()
+    out = ct.c_double(0.0)
+    rc = L.mfm_fm_eval_device(_lib.MFM_DTYPE_F64, 0, 16, 16, 16, 3, 0.0, 16, 16, 4, 16, None, 7,
+                              0.0, ct.byref(out), None)
+    assert rc == _lib.MFM_ERR_INVALID and "unknown loss 7" in _lib.last_error()
+    rc = L.mfm_fm_eval_device(5, 0, 16, 16, 16, 3, 0.0, 16, 16, 4, 16, None, 0, 0.0,
+                              ct.byref(out), None)
+    assert rc == _lib.MFM_ERR_INVALID and "unknown dtype 5" in _lib.last_error()
+    # no rows: NumPy's mean of nothing (nan), answered before any device work
+    rc = L.mfm_fm_eval_device(_lib.MFM_DTYPE_F64, 0, None, None, None, 0, 0.0, None, None, 4,
+                              None, None, 0, 0.0, ct.byref(out), None)
+    assert rc == _lib.MFM_OK and np.isnan(out.value)
