@@ -207,6 +207,28 @@ int mfm_csr_prep_device(int dtype, int device, int64_t n_rows, int64_t n_feature
                         int64_t* indptr_out, int32_t* indices_out, void* data_out,
                         int64_t* nnz_out, void* stream);
 
+/* ---- libffm text reader ---------------------------------------------------
+ * Replaces the reading half of the reference's load_libffm
+ * (python/modern_fm/libffm.py:31-83): parses a libffm file
+ * (`<label> <field>:<feature>:<value> ...` per line) on the host with
+ * n_threads threads (<= 0: every core) into a raw CSR in the boundary format:
+ * rows in file order, entries in token order, duplicates kept (the reference
+ * sums them when it builds its CSR; mfm_csr_prep_device does that on the
+ * device), float64 labels, and an int64 field id per feature (n_features =
+ * largest feature + 1; features never seen get field 0, as in the reference).
+ * Values are correctly rounded, as Python's float() reads them. Errors return
+ * MFM_ERR_INVALID with the reference's messages and line numbers ("path:line:
+ * bad token ...; expected field:feature:value", "negative field/feature in",
+ * "feature F maps to fields A and B", "could not convert string to float");
+ * features beyond 2^31-1 return MFM_ERR_UNSUPPORTED. The arrays belong to the
+ * handle: mfm_libffm_arrays gives pointers valid until mfm_libffm_free. */
+typedef struct mfm_libffm mfm_libffm;
+int mfm_libffm_read(const char* path, int n_threads, mfm_libffm** out);
+int mfm_libffm_info(const mfm_libffm* f, int64_t* n_rows, int64_t* nnz, int64_t* n_features);
+int mfm_libffm_arrays(const mfm_libffm* f, const int64_t** indptr, const int64_t** indices,
+                      const double** data, const double** y, const int64_t** field_ids);
+void mfm_libffm_free(mfm_libffm* f);
+
 /* ---- early-stopping evaluation on the device -----------------------------
  * Replaces the host evaluation the reference's early-stopped FM fits run after
  * every epoch, `metric(y_val, fm_predict_fast(X_val, w0, w, V))`

@@ -98,6 +98,10 @@ _SIGNATURES = {
                                       ct.c_int64, ct.c_double, ct.c_void_p, ct.c_void_p,
                                       ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_double,
                                       f64p, ct.c_void_p]),
+    "mfm_libffm_read": (ct.c_int, [ct.c_char_p, ct.c_int, ct.POINTER(ct.c_void_p)]),
+    "mfm_libffm_info": (ct.c_int, [ct.c_void_p, i64p, i64p, i64p]),
+    "mfm_libffm_arrays": (ct.c_int, [ct.c_void_p] + [ct.POINTER(ct.c_void_p)] * 5),
+    "mfm_libffm_free": (None, [ct.c_void_p]),
     "mfm_fm_predict_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_double, ct.c_void_p,
                                          ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_void_p]),

@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ from the reference's NumPy
 ground truth (modern_fm v1.1.1, python/modern_fm/_reference.py and
-_reference_train.py), its CSR preparation (_backend._prep_csr) and its
-validation metrics (losses.py).
+_reference_train.py), its CSR preparation (_backend._prep_csr), its validation metrics
+(losses.py) and its libffm reader (libffm.py).
 
 Run in a container where the reference source tree is present:
 
@@ -300,7 +300,66 @@ def make_losses(L):
     w.save("losses.npz")
 
 
-MAKERS = ("predict", "train_binary", "train_multiclass", "prep", "losses")
+def make_libffm(LF):
+    """The reference's load_libffm (python/modern_fm/libffm.py:31-83) on seeded
+    libffm texts: its canonical X, y and field_ids, or the message of the
+    ValueError it raises (the file path replaced by "{path}")."""
+    import tempfile
+
+    w = Writer()
+    rng = np.random.default_rng(9)
+
+    def random_text(n, m, nl, sep, dups):
+        fields = rng.integers(0, 7, size=m)
+        lines = []
+        for _ in range(n):
+            L = int(rng.integers(0, 12))
+            toks = [repr(float(rng.integers(0, 2)))]
+            js = rng.integers(0, m, size=L)
+            if dups and L > 2:
+                js[-1] = js[0]  # one duplicate: exact sums
+            for j in js:
+                v = rng.normal()
+                sv = repr(float(v)) if rng.random() < 0.7 else "%.3e" % v
+                toks.append(f"{fields[j]}:{j}:{sv}")
+            lines.append(sep.join(toks))
+        return nl.join(lines) + nl
+
+    texts = {
+        "known": "1 0:0:1 1:2:0.5\n0 0:1:1 1:2:2\n",  # tests/test_libffm.py:9-17
+        "random_lf": random_text(400, 300, "\n", " ", False),
+        "random_crlf_blank": "\r\n" + random_text(300, 200, "\r\n", "\t", False) + "\r\n",
+        "random_cr": random_text(300, 200, "\r", "  ", False),
+        "dups": random_text(300, 50, "\n", " ", True),
+        "specials": "1 0:0:nan 1:1:-inf 2:2:1e400 3:3:.5 4:4:5. 5:1_0:2_5.0_1e-0_3\n0 6:6:+7\n",
+        "err_token": "1 0:0:1 not_a_triple\n",  # tests/test_libffm.py:58-62
+        "err_conflict": "1 0:0:1\n\n0 1:0:2\n",
+        "err_negative": "1 0:-1:1\n",
+        "err_label": "abc 0:0:1\n",
+        "err_four_parts": "1 0:0:1:2\n",
+        "err_int": "1 0:0:1 0:x:1\n",
+        "err_underscores": "1 0:0:1__0\n",
+        "err_hex": "1 0:0:0x10\n",
+        "err_conflict_before_token": "1 0:0:1 1:0:1 bad\n",
+    }
+    d = tempfile.mkdtemp()
+    for name, text in texts.items():
+        path = os.path.join(d, name + ".ffm")
+        with open(path, "w", newline="") as fh:
+            fh.write(text)
+        raw = np.frombuffer(text.encode(), dtype=np.uint8)
+        try:
+            X, y, f = LF.load_libffm(path)
+        except ValueError as e:
+            w.add(name, dict(error=str(e).replace(path, "{path}")), text=raw)
+            continue
+        w.add(name, dict(error=None, n_features=int(X.shape[1])), text=raw,
+              indptr=X.indptr.astype(np.int64), indices=X.indices.astype(np.int64), data=X.data,
+              y=y, field_ids=f)
+    w.save("libffm.npz")
+
+
+MAKERS = ("predict", "train_binary", "train_multiclass", "prep", "losses", "libffm")
 
 
 def main():
@@ -314,6 +373,7 @@ def main():
     from modern_fm import _backend as B  # noqa: E402
     from modern_fm import _reference as R  # noqa: E402
     from modern_fm import _reference_train as T  # noqa: E402
+    from modern_fm import libffm as LF  # noqa: E402
     from modern_fm import losses as L  # noqa: E402
 
     if "predict" in args.only:
@@ -326,6 +386,8 @@ def main():
         make_prep(B)
     if "losses" in args.only:
         make_losses(L)
+    if "libffm" in args.only:
+        make_libffm(LF)
 
 
 if __name__ == "__main__":
