@@ -96,3 +96,31 @@ def test_chunked_errors_report_the_first_in_file_order(tmp_path, kind):
 def test_missing_file_is_value_error(tmp_path):
     with pytest.raises(ValueError, match="cannot open"):
         read_libffm_raw(tmp_path / "nope.ffm")
+
+
+def test_values_round_like_python_float(tmp_path):
+    """Every value equals Python's float() of its literal bitwise (the
+    reference's reader calls float(), libffm.py:59): round-trip reprs across
+    magnitudes, %g / %e forms of 1-20 digits, long digit strings with large
+    exponents (correct rounding beyond the exact fast path), underscores,
+    subnormals and overflow."""
+    rng = np.random.default_rng(5)
+    vals = []
+    for _ in range(8000):
+        x = float(rng.normal() * 10.0 ** rng.integers(-30, 30))
+        vals += [repr(x), "%.*g" % (int(rng.integers(1, 18)), x),
+                 "%.*e" % (int(rng.integers(0, 20)), x)]
+    for _ in range(3000):
+        vals.append(str(int(rng.integers(-10**18, 10**18))))
+        vals.append("0." + "".join(map(str, rng.integers(0, 10, size=int(rng.integers(1, 25))))))
+        vals.append("".join(map(str, rng.integers(0, 10, size=int(rng.integers(1, 25)))))
+                    + "e" + str(int(rng.integers(-330, 310))))
+    vals += ["1_000.5", "1_0e1_0", ".5", "5.", "-0", "+0.0", "1e-400", "4.9406564584124654e-324",
+             "2.2250738585072011e-308", "9007199254740993", "0.1", "1e22", "1e23",
+             "123456789012345e-22", "1234567890123456e-22", "-INF", "Infinity", "1.7976931348623159e308"]
+    p = tmp_path / "v.ffm"
+    p.write_text("".join("1 " + " ".join(f"0:{i + k}:{v}" for k, v in enumerate(vals[i:i + 10]))
+                         + "\n" for i in range(0, len(vals), 10)))
+    _, _, dv, _, _, _ = read_libffm_raw(p, 4)
+    want = np.array([float(v) for v in vals])
+    assert np.array_equal(dv.view(np.int64), want.view(np.int64))
