@@ -12,7 +12,10 @@ over ranks); `e2e` is the same metric through the reference-facing C ABI
 indices, float64 values and parameters) — host->device copies, validation,
 conversion and the device->host read of the scores all inside the timed region.
 `--impl reference` times the reference's CPU engine (its C restatement, rows
-split over every host core) on the same configuration.
+split over every host core) on the same configuration. The line also carries
+`train` (one 10M-row FM AdaGrad epoch; `train_dp` across ranks for N > 1) and
+`prep` (device CSR canonicalisation of the scoring batch in the boundary
+format, canonical and unsorted with duplicates).
 """
 
 from __future__ import annotations
