@@ -321,6 +321,7 @@ struct Chunk {
     // parsing pass
     int64_t lines = 0;                  // lines read (blank ones included)
     int64_t parsed_rows = 0, parsed_entries = 0;
+    int64_t max_feat = -1, max_field = -1;  // over the parsed entries
     // first error: chunk-local line, code, message (with or without the
     // reference's "path:line: " prefix)
     bool err = false, err_prefixed = false;
@@ -405,6 +406,8 @@ void parse_chunk(Chunk& C, const Sink& S) {
             S.field[k] = f;
             S.data[k] = x;
             ++k;
+            if (j > C.max_feat) C.max_feat = j;
+            if (f > C.max_field) C.max_field = f;
         }
         S.indptr[r + 1] = k;
         ++r;
@@ -493,26 +496,44 @@ void read_libffm(const char* path, int n_threads, mfm_libffm& out) {
 
     // file-order pass: each feature's field (libffm.py:65-69); the first error
     // in file order wins
-    int64_t max_feat = -1;
-    for (const Chunk& C : ch)
-        for (int64_t k = C.entry0; k < C.entry0 + C.parsed_entries; ++k)
-            max_feat = std::max(max_feat, out.indices[(size_t)k]);
+    int64_t max_feat = -1, max_field = -1;
+    for (const Chunk& C : ch) {
+        max_feat = std::max(max_feat, C.max_feat);
+        max_field = std::max(max_field, C.max_field);
+    }
     const bool dense = max_feat < (int64_t(1) << 25);  // else a hash map
-    std::vector<int64_t> fv(dense ? (size_t)(max_feat + 1) : 0, -1);
+    const bool narrow = max_field < INT32_MAX;         // 4-byte table entries
+    std::vector<int32_t> fv32(dense && narrow ? (size_t)(max_feat + 1) : 0, -1);
+    std::vector<int64_t> fv64(dense && !narrow ? (size_t)(max_feat + 1) : 0, -1);
     std::unordered_map<int64_t, int64_t> fm;
     int64_t line0 = 0;
     for (const Chunk& C : ch) {
-        int64_t r = C.row0;
-        for (int64_t k = C.entry0; k < C.entry0 + C.parsed_entries; ++k) {
-            while (out.indptr[(size_t)r + 1] <= k) ++r;  // the row holding entry k
-            const int64_t j = out.indices[(size_t)k], f = field[(size_t)k];
-            int64_t& slot = dense ? fv[(size_t)j] : fm.emplace(j, -1).first->second;
-            if (slot < 0) slot = f;
-            if (slot != f)
-                fail(MFM_ERR_INVALID,
-                     fmt("%s:%lld: feature %lld maps to fields %lld and %lld", path,
-                         (long long)(line0 + row_line[(size_t)r]), (long long)j, (long long)slot,
-                         (long long)f));
+        const int64_t k0 = C.entry0, k1 = C.entry0 + C.parsed_entries;
+        int64_t bad = -1, prev = -1;  // first conflicting entry and the field seen before
+        if (dense && narrow) {
+            for (int64_t k = k0; k < k1 && bad < 0; ++k) {
+                int32_t& slot = fv32[(size_t)out.indices[(size_t)k]];
+                const int32_t f = (int32_t)field[(size_t)k];
+                if (slot < 0) slot = f;
+                if (slot != f) bad = k, prev = slot;
+            }
+        } else {
+            for (int64_t k = k0; k < k1 && bad < 0; ++k) {
+                const int64_t j = out.indices[(size_t)k], f = field[(size_t)k];
+                int64_t& slot = dense ? fv64[(size_t)j] : fm.emplace(j, -1).first->second;
+                if (slot < 0) slot = f;
+                if (slot != f) bad = k, prev = slot;
+            }
+        }
+        if (bad >= 0) {
+            // the row holding entry `bad`: the last parsed row starting at or before it
+            const int64_t* ip = out.indptr.data();
+            const int64_t r = std::upper_bound(ip + C.row0 + 1, ip + C.row0 + C.parsed_rows + 1,
+                                               bad) - (ip + 1);
+            fail(MFM_ERR_INVALID,
+                 fmt("%s:%lld: feature %lld maps to fields %lld and %lld", path,
+                     (long long)(line0 + row_line[(size_t)r]), (long long)out.indices[(size_t)bad],
+                     (long long)prev, (long long)field[(size_t)bad]));
         }
         if (C.err)
             fail(C.err_code, C.err_prefixed ? fmt("%s:%lld: ", path,
@@ -526,9 +547,12 @@ void read_libffm(const char* path, int n_threads, mfm_libffm& out) {
     out.n_features = max_feat + 1;
     out.field_ids.alloc((size_t)out.n_features);
     std::fill(out.field_ids.data(), out.field_ids.data() + out.n_features, int64_t(0));
-    if (dense) {
+    if (dense && narrow) {
         for (int64_t j = 0; j < out.n_features; ++j)
-            if (fv[(size_t)j] >= 0) out.field_ids[(size_t)j] = fv[(size_t)j];
+            if (fv32[(size_t)j] >= 0) out.field_ids[(size_t)j] = fv32[(size_t)j];
+    } else if (dense) {
+        for (int64_t j = 0; j < out.n_features; ++j)
+            if (fv64[(size_t)j] >= 0) out.field_ids[(size_t)j] = fv64[(size_t)j];
     } else {
         for (const auto& kv : fm) out.field_ids[(size_t)kv.first] = kv.second;
     }
