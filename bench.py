@@ -15,7 +15,8 @@ conversion and the device->host read of the scores all inside the timed region.
 split over every host core) on the same configuration. The line also carries
 `train` (one 10M-row FM AdaGrad epoch; `train_dp` across ranks for N > 1) and
 `prep` (device CSR canonicalisation of the scoring batch in the boundary
-format, canonical and unsorted with duplicates).
+format, canonical and unsorted with duplicates) and, at N = 1, `libffm` (the
+native libffm reader on a CTR-shaped file, and loading it onto the GPU).
 """
 
 from __future__ import annotations
@@ -491,6 +492,71 @@ def prep_measure(args, local, dev_t, L, _lib, X):
     return res
 
 
+def libffm_measure(local, dev_t):
+    """The native libffm reader (mfm_libffm_read; the reference's load_libffm,
+    python/modern_fm/libffm.py:31-83, is pure Python) on a CTR-shaped file:
+    20,000 seeded rows of 39 `field:feature:value` tokens (13 numeric values
+    in %g form, 26 one-hot), written ten times over (200,000 rows). Times the
+    host read with every host thread and the full load onto the GPU (read,
+    upload, device canonicalisation); parity of the raw read against the
+    values written (Python's float() of each literal). Any failure is
+    reported in the line instead of the figures."""
+    import tempfile
+
+    import torch
+
+    from modern_fm_b200.libffm import load_libffm_device, read_libffm_raw
+
+    try:
+        rng = np.random.default_rng(SEED)
+        n0, z, reps = 20_000, NNZ_PER_ROW, 10
+        feat = np.sort(rng.integers(0, N_FEATURES, size=(n0, z)), axis=1)
+        fld = feat % z  # one field per feature, as the format requires
+        vals = np.where(np.arange(z)[None, :] < 13, np.round(rng.lognormal(0, 2, (n0, z)), 6), 1.0)
+        lab = (rng.random(n0) < 0.03).astype(np.int64)
+        vtxt = np.char.mod("%g", vals)
+        tok = np.char.add(np.char.add(np.char.add(np.char.add(fld.astype(str), ":"),
+                                                  feat.astype(str)), ":"), vtxt)
+        block = "".join(f"{lab[i]} " + " ".join(tok[i]) + "\n" for i in range(n0))
+        d = tempfile.mkdtemp()
+        path = os.path.join(d, "ctr.ffm")
+        with open(path, "w") as fh:
+            fh.write(block * reps)
+        size = os.path.getsize(path)
+        threads = os.cpu_count() or 1
+        host = []
+        for _ in range(3):
+            t = time.perf_counter()
+            ip, ix, dv, y, f, nf = read_libffm_raw(path, threads)
+            host.append(time.perf_counter() - t)
+        want_v = np.array([float(v) for v in vtxt.ravel()])
+        parity = bool(np.array_equal(ix[:n0 * z], feat.ravel())
+                      and np.array_equal(dv[:n0 * z].view(np.int64), want_v.view(np.int64))
+                      and np.array_equal(y[:n0], lab.astype(np.float64))
+                      and len(y) == n0 * reps and np.array_equal(ip[:n0 + 1], np.arange(n0 + 1) * z))
+        dev = []
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            out = load_libffm_device(path, dtype="float32", n_threads=threads, device=local)
+            torch.cuda.synchronize()
+            dev.append(time.perf_counter() - t)
+            del out
+        os.remove(path)
+        os.rmdir(d)
+        n = n0 * reps
+        h, g = statistics.median(host), statistics.median(dev)
+        return {"rows": n, "bytes": size, "threads": threads,
+                "host_read": {"s": h, "rows_per_s": n / h, "mb_per_s": size / h / 1e6},
+                "load_to_device": {"s": g, "rows_per_s": n / g, "mb_per_s": size / g / 1e6},
+                "parity": parity,
+                "workload": "20,000 seeded CTR-shaped rows (39 tokens: 13 numeric %g values, 26 "
+                            "one-hot) written ten times; host read with every host thread; load = "
+                            "read + upload + device canonicalisation (float32)"}
+    except Exception as exc:  # a failure here must not cost the rest of the line
+        return {"error": f"{type(exc).__name__}: {exc}"}
+
+
 def run_ours(args):
     import torch
 
@@ -605,6 +671,8 @@ def run_ours(args):
                          "single-threaded, rust/src/fm.rs:58-70)"}
 
     prep = None if args.no_prep else prep_measure(args, local, dev_t, L, _lib, X)
+    libffm = (libffm_measure(local, dev_t)
+              if rank == 0 and world == 1 and not args.no_libffm else None)
     train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
     train_dp = (train_dp_measure(args, rank, world, local, dev_t, L, _lib)
                 if world > 1 and not args.no_train else None)
@@ -635,6 +703,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if prep:
             line["prep"] = prep
+        if libffm:
+            line["libffm"] = libffm
         if train:
             line["train"] = train
         if train_dp:
@@ -799,6 +869,8 @@ def main():
     ap.add_argument("--train-only", action="store_true",
                     help="only the training measurement (profiling runs)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--no-libffm", action="store_true",
+                    help="skip the libffm reader measurement")
     ap.add_argument("--no-prep", action="store_true",
                     help="skip the device CSR canonicalisation measurement")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS)
