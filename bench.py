@@ -1,19 +1,25 @@
 """Benchmark: FM CSR scoring rows/s on B200 (the large CTR-shaped FM config:
-39 fields, 2^22 features, k=16, float32), with the HBM roofline fraction.
+39 fields, 2^22 features, k=16), with the HBM roofline fraction.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 One step = one scoring pass over one 2,000,000-row test batch per GPU (weak
 scaling: every rank scores its own seeded shard; rows are independent so no
-collective exists on this path). `value` is device-resident throughput (CSR,
-parameters and output already in HBM, CUDA events on the launch stream, max
-over ranks); `e2e` is the same metric through the reference-facing C ABI
-(mfm_fm_predict_csr) with pinned HOST buffers in the boundary format (int64
-indices, float64 values and parameters) — host->device copies, validation,
-conversion and the device->host read of the scores all inside the timed region.
+collective exists on this path). The arithmetic is the reference's: float64
+values, sums and scores on float32 parameters, as its default float32
+estimator computes (attributes stored float32, widened to float64 before its
+float64 kernels). `value` is device-resident throughput (CSR, parameters and
+output already in HBM, CUDA events on the launch stream, max over ranks);
+`e2e` is the same metric through the C ABI with pinned HOST buffers in the
+boundary format (int64 indices, float64 values): the model handle
+(mfm_model_predict_csr, parameters resident) as the headline and the
+reference-shaped stateless call (mfm_fm_predict_csr, parameters uploaded every
+call) beside it — host->device copies, validation and the device->host read of
+the scores all inside the timed region. `f32` is the float32-arithmetic figure.
 `--impl reference` times the reference's CPU engine (its C restatement, rows
 split over every host core) on the same configuration. The line also carries
-`train` (one 10M-row FM AdaGrad epoch; `train_dp` across ranks for N > 1) and
+`train` (one 10M-row FM AdaGrad epoch in float64, float32 beside it, parity of
+a float64 fit against the oracle; `train_dp` across ranks for N > 1) and
 `prep` (device CSR canonicalisation of the scoring batch in the boundary
 format, canonical and unsorted with duplicates) and, at N = 1, `libffm` (the
 native libffm reader on a CTR-shaped file, and loading it onto the GPU).
@@ -40,12 +46,15 @@ N_FEATURES = 2 ** 22
 K = 16
 NNZ_PER_ROW = 39
 SEED = 2
-# algorithmic bytes per row, float32 compute: indptr 8 + nnz*(idx 4 + val 4)
-# + nnz*(k+1)*4 (w and V gathers) + score 4
-BYTES_PER_ROW = 8 + NNZ_PER_ROW * 8 + NNZ_PER_ROW * (K + 1) * 4 + 4
+# algorithmic bytes per row, float32 parameters with float64 values and
+# scores: indptr 8 + nnz*(idx 4 + val 8) + nnz*(k+1)*4 (w and V gathers) + score 8
+BYTES_PER_ROW = 8 + NNZ_PER_ROW * 12 + NNZ_PER_ROW * (K + 1) * 4 + 8
+# float32 throughout: values 4 B, score 4 B
+BYTES_PER_ROW_F32 = 8 + NNZ_PER_ROW * 8 + NNZ_PER_ROW * (K + 1) * 4 + 4
 CONFIG = {
     "workload": "FM predict, CTR-shaped: 39 fields (13 numeric + 26 Zipf(1.1) hashed "
-                "categorical), 2^22 features, k=16, float32, 2,000,000 rows per GPU",
+                "categorical), 2^22 features, k=16, float32 parameters, float64 values and "
+                "arithmetic, 2,000,000 rows per GPU",
     "rows_per_gpu": N_ROWS, "n_features": N_FEATURES, "k": K, "nnz_per_row": NNZ_PER_ROW,
     "l2_policy": "inputs larger than L2 (CSR 624 MB + V 268 MB per GPU; L2 126 MB)",
 }
@@ -85,6 +94,8 @@ class ClockSampler:
         self.lines = []
 
     def __enter__(self):
+        if self.idx < 0:  # sampling off
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -205,21 +216,22 @@ TRAIN_BATCH = 4096
 
 
 def train_inputs(n, seed, dev_t, L, _lib):
-    """The training workload on the device: CTR-shaped CSR, labels drawn from a
-    planted FM with N(0, 0.1) parameters at ~3 % positives, unit sample
-    weights, one shuffled row order."""
+    """The training workload on the device: CTR-shaped CSR (float64 values),
+    labels drawn from a planted FM with N(0, 0.1) parameters at ~3 %
+    positives, unit sample weights, one shuffled row order, and the initial
+    latent factors N(0, 0.01) (float64)."""
     import torch
 
     from modern_fm_b200 import workloads as WL
 
-    X = WL.ctr_fm_torch(n, seed, device=dev_t)
+    X = WL.ctr_fm_torch(n, seed, device=dev_t, value_dtype=torch.float64)
     g = torch.Generator(device=dev_t)
     g.manual_seed(seed + 4219)
     wp = (torch.randn(N_FEATURES, generator=g, device=dev_t) * 0.1).contiguous()
     Vp = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.1).contiguous()
-    sc = torch.empty(n, dtype=torch.float32, device=dev_t)
+    sc = torch.empty(n, dtype=torch.float64, device=dev_t)
     stream = torch.cuda.current_stream(dev_t)
-    rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32, dev_t.index, X["indptr"].data_ptr(),
+    rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32_F64, dev_t.index, X["indptr"].data_ptr(),
                                  X["indices"].data_ptr(), X["data"].data_ptr(), n, 0.0,
                                  wp.data_ptr(), Vp.data_ptr(), K, sc.data_ptr(), stream.cuda_stream)
     if rc:
@@ -227,29 +239,66 @@ def train_inputs(n, seed, dev_t, L, _lib):
     lo, hi = -50.0, 50.0
     for _ in range(60):
         mid = 0.5 * (lo + hi)
-        if float(torch.sigmoid(sc.double() + mid).mean()) > 0.03:
+        if float(torch.sigmoid(sc + mid).mean()) > 0.03:
             hi = mid
         else:
             lo = mid
-    y = (torch.rand(n, generator=g, device=dev_t) < torch.sigmoid(sc + 0.5 * (lo + hi))).float()
-    sw = torch.ones(n, device=dev_t)
+    y = (torch.rand(n, generator=g, device=dev_t, dtype=torch.float64)
+         < torch.sigmoid(sc + 0.5 * (lo + hi))).double()
+    sw = torch.ones(n, device=dev_t, dtype=torch.float64)
     order = torch.randperm(n, generator=g, device=dev_t).to(torch.int32).contiguous()
-    V0 = (torch.randn(N_FEATURES, K, generator=g, device=dev_t) * 0.01).contiguous()
+    V0 = (torch.randn(N_FEATURES, K, generator=g, device=dev_t, dtype=torch.float64)
+          * 0.01).contiguous()
     return X, y, sw, order, V0
+
+
+def _tr_adagrad(_lib, row_orders=None, n_epochs=1):
+    return _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
+                      1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, row_orders, n_epochs, TRAIN_BATCH)
+
+
+def _device_fit(L, _lib, dtype, local, X, y, sw, order, n, V0, stream):
+    """One epoch per call of mfm_fm_fit_device on fresh zero-initialised
+    w / state and the given V (all in `dtype`). Returns (epoch, w0, w, V)."""
+    import torch
+
+    tdt = torch.float32 if dtype == _lib.MFM_DTYPE_F32 else torch.float64
+    data = X["data"].to(tdt)
+    yt, swt = y.to(tdt), sw.to(tdt)
+    w0 = torch.zeros(1, device=V0.device, dtype=tdt)
+    w = torch.zeros(N_FEATURES, device=V0.device, dtype=tdt)
+    V = V0.to(tdt).clone()
+    acc0, accw, accV = torch.zeros_like(w0), torch.zeros_like(w), torch.zeros_like(V)
+    tr = _tr_adagrad(_lib)
+    grp = [_lib.DevGroup(p.data_ptr(), a.data_ptr(), None, None, None, None, None)
+           for p, a in ((w0, acc0), (w, accw), (V, accV))]
+
+    def epoch():
+        rc = L.mfm_fm_fit_device(dtype, local, X["indptr"].data_ptr(), X["indices"].data_ptr(),
+                                 data.data_ptr(), n, N_FEATURES, yt.data_ptr(), swt.data_ptr(),
+                                 order.data_ptr(), tr, K, grp[0], grp[1], grp[2],
+                                 stream.cuda_stream)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    return epoch, w0, w, V, (data, yt, swt, acc0, accw, accV, tr, grp)
 
 
 def train_measure(args, rank, world, local, dev_t, L, _lib):
     """FM AdaGrad training on the large CTR config: 10M rows, batch 4096,
-    k=16, float32, one epoch per step. Returns the `train` object of the
-    JSON line (rank 0) or None."""
+    k=16, one epoch per step, in float64 (the reference's training
+    arithmetic: float64 parameters and state for the whole fit,
+    python/modern_fm/_backend.py:116-130), with float32 as a secondary figure.
+    Returns the `train` object of the JSON line (rank 0) or None."""
     import torch
 
     n = args.train_rows
     X, y, sw, order, V0 = train_inputs(n, SEED + 100 + rank, dev_t, L, _lib)
     stream = torch.cuda.current_stream(dev_t)
-    # algorithmic bytes of one epoch: per row the scoring gathers (2976 B) + y,
-    # sample weight; per (batch, touched feature) param and AdaGrad state read
-    # and written: 4 x (k+1) x 4 B
+    # algorithmic bytes of one epoch (s = bytes per parameter / value): per row
+    # indptr 8, per entry index 4 + value s + (w, V) gathers (k+1) s, label and
+    # sample weight 2 s; per (batch, touched feature) parameter and AdaGrad
+    # state read and written: 4 (k+1) s
     rows_of = torch.repeat_interleave(
         torch.arange(n, device=dev_t), X["indptr"][1:] - X["indptr"][:-1])
     pos_of = torch.empty(n, dtype=torch.int64, device=dev_t)
@@ -257,49 +306,45 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     keys = (pos_of[rows_of] // TRAIN_BATCH) * N_FEATURES + X["indices"].long()
     touched = int(torch.unique(keys).numel())
     del rows_of, pos_of, keys
-    bytes_epoch = n * (BYTES_PER_ROW - 4 + 8) + touched * (K + 1) * 4 * 4
+    nnz = int(X["indices"].numel())
 
-    w0 = torch.zeros(1, device=dev_t)
-    w = torch.zeros(N_FEATURES, device=dev_t)
-    V = V0
-    acc0, accw, accV = torch.zeros(1, device=dev_t), torch.zeros_like(w), torch.zeros_like(V)
-    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
-                    1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, None, 1, TRAIN_BATCH)
-    grp = [_lib.DevGroup(p.data_ptr(), a.data_ptr(), None, None, None, None, None)
-           for p, a in ((w0, acc0), (w, accw), (V, accV))]
+    def bytes_epoch(sz):
+        return n * 8 + nnz * (4 + sz + (K + 1) * sz) + n * 2 * sz + touched * (K + 1) * sz * 4
 
-    def epoch():
-        rc = L.mfm_fm_fit_device(_lib.MFM_DTYPE_F32, local, X["indptr"].data_ptr(),
-                                 X["indices"].data_ptr(), X["data"].data_ptr(), n, N_FEATURES,
-                                 y.data_ptr(), sw.data_ptr(), order.data_ptr(), tr, K, grp[0],
-                                 grp[1], grp[2], stream.cuda_stream)
-        if rc:
-            raise RuntimeError(_lib.last_error())
+    def run(dtype, steps):
+        epoch, w0, w, V, keep = _device_fit(L, _lib, dtype, local, X, y, sw, order, n, V0,
+                                            stream)
+        epoch()  # warm-up: allocator and module load
+        torch.cuda.synchronize()
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
+            epoch()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(t0.elapsed_time(t1) / steps, world)
+        if not np.isfinite(float(V.abs().max())):
+            raise RuntimeError("training diverged")
+        return ms
 
-    epoch()  # warm-up: allocator and module load
-    torch.cuda.synchronize()
-    barrier(world)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(args.train_steps):
-        epoch()
-    t1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(t0.elapsed_time(t1) / args.train_steps, world)
-    if not np.isfinite(float(V.abs().max())):
-        raise RuntimeError("training diverged")
-
+    ms = run(_lib.MFM_DTYPE_F64, args.train_steps)
+    ms32 = run(_lib.MFM_DTYPE_F32, args.train_steps)
+    peak, _ = peaks()
+    b64, b32 = bytes_epoch(8), bytes_epoch(4)
     out = {
         "metric": "FM AdaGrad training rows/s (CTR-shaped 39 fields, 2^22 features, k=16, "
                   "batch 4096, 1 epoch per step)",
-        "value": world * n / (ms / 1e3), "unit": "rows/s", "rows_per_gpu": n,
+        "value": world * n / (ms / 1e3), "unit": "rows/s", "rows_per_gpu": n, "dtype": "f64",
         "steps": args.train_steps, "ms_per_step": ms, "scaling": "weak (independent fits)",
+        "roofline": {"bound": "hbm", "achieved": b64 / (ms / 1e3) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": b64 / (ms / 1e3) / 1e9 / peak,
+                     "bytes_per_epoch": b64, "touched_per_epoch": touched},
+        "f32": {"value": world * n / (ms32 / 1e3), "unit": "rows/s", "ms_per_step": ms32,
+                "dtype": "f32", "roofline": {"achieved": b32 / (ms32 / 1e3) / 1e9,
+                                             "frac": b32 / (ms32 / 1e3) / 1e9 / peak,
+                                             "bytes_per_epoch": b32}},
     }
-    peak, _ = peaks()
-    achieved = bytes_epoch / (ms / 1e3) / 1e9
-    out["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                       "frac": achieved / peak, "bytes_per_epoch": bytes_epoch,
-                       "touched_per_epoch": touched}
     if args.train_e2e_rows <= 0:
         return out if rank == 0 else None
 
@@ -308,21 +353,19 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     n_e = min(n, args.train_e2e_rows)
     ip = X["indptr"][: n_e + 1].cpu().pin_memory()
     ix = X["indices"][: int(ip[-1])].to(torch.int64).cpu().pin_memory()
-    dv = X["data"][: int(ip[-1])].to(torch.float64).cpu().pin_memory()
-    yh = y[:n_e].double().cpu().pin_memory()
+    dv = X["data"][: int(ip[-1])].cpu().pin_memory()
+    yh = y[:n_e].cpu().pin_memory()
     swh = torch.ones(n_e, dtype=torch.float64).pin_memory()
     roh = torch.arange(n_e, dtype=torch.int64).reshape(1, -1).pin_memory()
     wh = torch.zeros(N_FEATURES, dtype=torch.float64).pin_memory()
-    Vh = V.double().cpu().pin_memory()
+    Vh = V0.cpu().pin_memory()
     awh, aVh = torch.zeros_like(wh).pin_memory(), torch.zeros_like(Vh).pin_memory()
     csr, keep = _lib.make_csr(ip.numpy(), ix.numpy(), dv.numpy(), N_FEATURES)
-    tr_h = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
-                      1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, _lib.ptr(roh.numpy(), _lib.i64p), 1,
-                      TRAIN_BATCH)
+    tr_h = _tr_adagrad(_lib, _lib.ptr(roh.numpy(), _lib.i64p), 1)
     w0a, a0a = np.zeros(1), np.zeros(1)
     gh = [_lib.Group(_lib.ptr(p), _lib.ptr(a), None, None, None, None, None)
           for p, a in ((w0a, a0a), (wh.numpy(), awh.numpy()), (Vh.numpy(), aVh.numpy()))]
-    ex = _lib.Exec(_lib.MFM_DTYPE_F32, local, 1)
+    ex = _lib.Exec(_lib.MFM_DTYPE_F64, local, 1)
 
     def e2e_fit():
         rc = L.mfm_fm_fit_csr(csr, _lib.ptr(yh.numpy()), _lib.ptr(swh.numpy()), tr_h, K, gh[0],
@@ -338,56 +381,79 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
     h2d = sum(a.numpy().nbytes for a in (ip, ix, dv, yh, swh, roh, wh, Vh, awh, aVh)) + 16
     d2h = sum(a.numpy().nbytes for a in (wh, Vh, awh, aVh)) + 16
 
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import oracle as O
 
+        # the oracle's fit (n_jobs = every host thread) of the first n_c rows,
+        # one epoch in row order, and the engine's float64 fit of the same rows
         n_c = args.train_cpu_rows
         ipc = ip.numpy()[: n_c + 1]
         nzc = int(ipc[-1])
         threads = os.cpu_count() or 1
-        wc, Vc = np.zeros(N_FEATURES), V.double().cpu().numpy()
+        wc, Vc = np.zeros(N_FEATURES), V0.cpu().numpy().copy()
+        awc, aVc = np.zeros(N_FEATURES), np.zeros_like(Vc)
         t = time.perf_counter()
-        O.fm_fit_csr(ipc, ix.numpy()[:nzc], dv.numpy()[:nzc], N_FEATURES, yh.numpy()[:n_c],
-                     np.ones(n_c), 0.0, 0.0, wc, Vc, np.zeros(N_FEATURES), np.zeros_like(Vc),
-                     "logistic", "adagrad", 0.05, 1e-5, 1e-5, 0.9, 0.999, 1e-8,
-                     np.arange(n_c)[None, :], TRAIN_BATCH, threads, 0.0, 0.0, 1.0)
+        r0 = O.fm_fit_csr(ipc, ix.numpy()[:nzc], dv.numpy()[:nzc], N_FEATURES, yh.numpy()[:n_c],
+                          np.ones(n_c), 0.0, 0.0, wc, Vc, awc, aVc, "logistic", "adagrad", 0.05,
+                          1e-5, 1e-5, 0.9, 0.999, 1e-8, np.arange(n_c)[None, :], TRAIN_BATCH,
+                          threads, 0.0, 0.0, 1.0)
         cpu = {"value": n_c / (time.perf_counter() - t), "unit": "rows/s", "cores": threads,
                "kind": "port", "sample": f"first {n_c} rows, one epoch, n_jobs={threads} "
                                          "(contiguous-chunk split, rust/src/fm.rs:286-311)"}
+        Xc = dict(indptr=X["indptr"][: n_c + 1].contiguous(), indices=X["indices"][:nzc],
+                  data=X["data"][:nzc])
+        oc = torch.arange(n_c, dtype=torch.int32, device=dev_t)
+        epoch, w0g, wg, Vg, keep_c = _device_fit(L, _lib, _lib.MFM_DTYPE_F64, local, Xc,
+                                                 y[:n_c], sw[:n_c], oc, n_c, V0, stream)
+        epoch()
+        torch.cuda.synchronize()
+        wg, Vg = wg.cpu().numpy(), Vg.cpu().numpy()
+        ok_w = np.allclose(wg, wc, rtol=1e-7, atol=1e-9)
+        ok_v = np.allclose(Vg, Vc, rtol=1e-7, atol=1e-9)
+        ok_w0 = abs(float(w0g.item()) - r0[0]) <= 1e-7 * abs(r0[0]) + 1e-9
+        parity = {"ok": bool(ok_w and ok_v and ok_w0), "rows": n_c,
+                  "max_abs_dw": float(np.abs(wg - wc).max()),
+                  "max_abs_dV": float(np.abs(Vg - Vc).max()),
+                  "tolerance": "float64 fit of the first rows against the oracle's fit: "
+                               "rtol 1e-7, atol 1e-9 on w0, w and V"}
     if rank != 0:
         return None
-    out["e2e"] = {"value": world * n_e / e2e_s, "unit": "rows/s", "rows": n_e,
+    out["e2e"] = {"value": world * n_e / e2e_s, "unit": "rows/s", "rows": n_e, "dtype": "f64",
                   "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
     if cpu:
         out["cpu_baseline"] = cpu
+    if parity:
+        out["parity"] = parity
     return out
 
 
 def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
     """One data-parallel fit across all ranks (N > 1): the same 10M-row epoch,
     every global batch of 4096 rows split over the ranks, one allreduce of the
-    batch's per-key gradient sums per batch. Strong scaling of one fit."""
+    batch's per-key gradient sums per batch, in float64. Parity: rank 0 also
+    fits the same epochs on its own GPU alone and compares."""
     import torch
 
     from modern_fm_b200 import dp as DP
 
     n = args.train_rows
-    X, y, sw, order, V = train_inputs(n, SEED + 100, dev_t, L, _lib)  # same data on every rank
+    X, y, sw, order, V0 = train_inputs(n, SEED + 100, dev_t, L, _lib)  # same data on every rank
     stream = torch.cuda.current_stream(dev_t)
-    w0, w = torch.zeros(1, device=dev_t), torch.zeros(N_FEATURES, device=dev_t)
-    acc0, accw, accV = torch.zeros(1, device=dev_t), torch.zeros_like(w), torch.zeros_like(V)
-    tr = _lib.Train(_lib.LOSSES["logistic"], _lib.OPTIMIZERS["adagrad"], 0.05, 0.0, 1e-5, 0.0,
-                    1e-5, 0.9, 0.999, 1e-8, 1.0, 0.0, None, 1, TRAIN_BATCH)
+    dt = _lib.MFM_DTYPE_F64
+    w0, w, V = (torch.zeros(1, device=dev_t, dtype=torch.float64),
+                torch.zeros(N_FEATURES, device=dev_t, dtype=torch.float64), V0.clone())
+    acc0, accw, accV = torch.zeros_like(w0), torch.zeros_like(w), torch.zeros_like(V)
+    tr = _tr_adagrad(_lib)
     grp = [_lib.DevGroup(p.data_ptr(), a.data_ptr(), None, None, None, None, None)
            for p, a in ((w0, acc0), (w, accw), (V, accV))]
     group = DP.DataParallelGroup(device=local)
     try:
         def epoch():
-            group.fm_fit_device(_lib.MFM_DTYPE_F32, X["indptr"].data_ptr(),
-                                X["indices"].data_ptr(), X["data"].data_ptr(), n, N_FEATURES,
-                                y.data_ptr(), sw.data_ptr(), order.data_ptr(), tr, K, grp[0],
-                                grp[1], grp[2], stream.cuda_stream)
+            group.fm_fit_device(dt, X["indptr"].data_ptr(), X["indices"].data_ptr(),
+                                X["data"].data_ptr(), n, N_FEATURES, y.data_ptr(),
+                                sw.data_ptr(), order.data_ptr(), tr, K, grp[0], grp[1], grp[2],
+                                stream.cuda_stream)
 
         epoch()
         torch.cuda.synchronize()
@@ -401,15 +467,31 @@ def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
         ms = max_over_ranks(t0.elapsed_time(t1) / args.train_steps, world)
     finally:
         group.close()
+    parity = None
+    if rank == 0:
+        one, w0s, ws, Vs, keep = _device_fit(L, _lib, dt, local, X, y, sw, order, n, V0, stream)
+        for _ in range(1 + args.train_steps):
+            one()
+        torch.cuda.synchronize()
+        dv_ = float((V - Vs).abs().max())
+        ok = bool(torch.allclose(V, Vs, rtol=1e-7, atol=1e-9)
+                  and torch.allclose(w, ws, rtol=1e-7, atol=1e-9)
+                  and torch.allclose(w0, w0s, rtol=1e-7, atol=1e-9))
+        parity = {"ok": ok, "max_abs_dV": dv_,
+                  "tolerance": "rank 0's parameters after the data-parallel epochs against a "
+                               "one-GPU fit of the same epochs: rtol 1e-7, atol 1e-9 (float64, "
+                               "sums in another order)"}
+    barrier(world)
     if rank != 0:
         return None
     return {"metric": "FM AdaGrad data-parallel training rows/s (one fit, global batch 4096 "
                       "split over the ranks, NCCL allreduce per batch)",
             "value": n / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "rows": n,
-            "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong"}
+            "dtype": "f64", "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong",
+            "parity": parity}
 
 
-PREP_BYTES_PER_ENTRY = 8 + 8 + 4 + 4  # int64 + float64 read, int32 + float32 written
+PREP_BYTES_PER_ENTRY = 8 + 8 + 4 + 8  # int64 + float64 read, int32 + float64 written
 PREP_BYTES_PER_ROW = 8 + 8            # indptr read and written
 
 
@@ -441,14 +523,14 @@ def prep_measure(args, local, dev_t, L, _lib, X):
     ix_raw[mid[has]] = ix_raw[ip[:-1][has]]
     ip_out = torch.empty(n + 1, dtype=torch.int64, device=dev_t)
     ix_out = torch.empty(nnz, dtype=torch.int32, device=dev_t)
-    dv_out = torch.empty(nnz, dtype=torch.float32, device=dev_t)
+    dv_out = torch.empty(nnz, dtype=torch.float64, device=dev_t)
     stream = torch.cuda.current_stream(dev_t)
     res = {}
     for name, (a, b) in (("canonical", (ix, dv)), ("unsorted_dup", (ix_raw, dv_raw))):
         m = ct.c_int64(0)
 
         def call():
-            rc = L.mfm_csr_prep_device(_lib.MFM_DTYPE_F32, local, n, N_FEATURES, nnz,
+            rc = L.mfm_csr_prep_device(_lib.MFM_DTYPE_F32_F64, local, n, N_FEATURES, nnz,
                                        ip.data_ptr(), a.data_ptr(), b.data_ptr(),
                                        ip_out.data_ptr(), ix_out.data_ptr(), dv_out.data_ptr(),
                                        ct.byref(m), stream.cuda_stream)
@@ -466,7 +548,7 @@ def prep_measure(args, local, dev_t, L, _lib, X):
         ev[1].record(stream)
         torch.cuda.synchronize()
         ms = ev[0].elapsed_time(ev[1]) / steps
-        algo = n * PREP_BYTES_PER_ROW + nnz * (8 + 8) + m.value * (4 + 4)
+        algo = n * PREP_BYTES_PER_ROW + nnz * (8 + 8) + m.value * (4 + 8)
         from oracle import oracle as O
 
         rows = 2000
@@ -477,7 +559,7 @@ def prep_measure(args, local, dev_t, L, _lib, X):
         mm = int(got_ip[-1])
         parity = bool(np.array_equal(got_ip, want[0])
                       and np.array_equal(ix_out[:mm].cpu().numpy().astype(np.int64), want[1])
-                      and np.array_equal(dv_out[:mm].cpu().numpy(), want[2].astype(np.float32)))
+                      and np.array_equal(dv_out[:mm].cpu().numpy(), want[2]))
         res[name] = {"rows_per_s": n / (ms / 1e3), "ms_per_call": ms, "nnz_in": nnz,
                      "nnz_out": m.value, "achieved_gbs": algo / (ms / 1e3) / 1e9,
                      "algorithmic_bytes": algo, "parity": parity}
@@ -486,7 +568,7 @@ def prep_measure(args, local, dev_t, L, _lib, X):
         v["frac"] = v["achieved_gbs"] / peak
     res["peak_gbs"], res["peak_kind"] = peak, kind
     res["bytes"] = ("indptr 8 read + 8 written per row; per input entry int64 column + float64 "
-                    "value read; per output entry int32 column + float32 value written")
+                    "value read; per output entry int32 column + float64 value written")
     res["workload"] = ("the 2,000,000-row scoring batch in the boundary format (int64 / "
                        "float64), canonical and with rows reversed plus one duplicate per row")
     return res
@@ -582,83 +664,115 @@ def run_ours(args):
 
             dist.destroy_process_group()
         return
-    X = WL.ctr_fm_torch(N_ROWS, SEED + rank, device=dev_t)
+    X = WL.ctr_fm_torch(N_ROWS, SEED + rank, device=dev_t, value_dtype=torch.float64)
+    X32 = dict(X, data=X["data"].float())
     w0, w64, V64 = make_params(local, dev_t)
+    # float32 parameters (a float32 estimator's attributes), float64 values
     w32, V32 = w64.float().contiguous(), V64.float().contiguous()
-    out = torch.empty(N_ROWS, dtype=torch.float32, device=dev_t)
+    out = torch.empty(N_ROWS, dtype=torch.float64, device=dev_t)
+    out32 = torch.empty(N_ROWS, dtype=torch.float32, device=dev_t)
     stream = torch.cuda.current_stream(dev_t)
 
-    def step():
-        rc = L.mfm_fm_predict_device(_lib.MFM_DTYPE_F32, local, X["indptr"].data_ptr(),
-                                     X["indices"].data_ptr(), X["data"].data_ptr(), N_ROWS, w0,
-                                     w32.data_ptr(), V32.data_ptr(), K, out.data_ptr(),
+    def step(dtype=_lib.MFM_DTYPE_F32_F64):
+        src, o = (X32, out32) if dtype == _lib.MFM_DTYPE_F32 else (X, out)
+        rc = L.mfm_fm_predict_device(dtype, local, src["indptr"].data_ptr(),
+                                     src["indices"].data_ptr(), src["data"].data_ptr(), N_ROWS,
+                                     w0, w32.data_ptr(), V32.data_ptr(), K, o.data_ptr(),
                                      stream.cuda_stream)
         if rc:
             raise RuntimeError(_lib.last_error())
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for i in range(args.steps):
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        t1.record(stream)
+    def timed(dtype, steps, clocks=False):
+        """(total ms, mean launch ms, clock summary) of `steps` device steps."""
+        for _ in range(max(3, args.warmup)):
+            step(dtype)
         torch.cuda.synchronize()
-    barrier(world)
-    total_ms = max_over_ranks(t0.elapsed_time(t1), world)
-    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
-    launch_ms = max_over_ranks(launch_ms, world)
-    clocks = clk.summary()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local if clocks else -1) as clk:
+            if clocks:
+                time.sleep(0.5)  # let nvidia-smi start sampling before the timed region
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            for i in range(steps):
+                starts[i].record(stream)
+                step(dtype)
+                ends[i].record(stream)
+            t1.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        total = max_over_ranks(t0.elapsed_time(t1), world)
+        launch = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends)),
+                                world)
+        return total, launch, clk.summary() if clocks else None
+
+    total_ms, launch_ms, clocks = timed(_lib.MFM_DTYPE_F32_F64, args.steps, clocks=True)
     if args.kernel_only:
         if rank == 0:
             print(json.dumps({"kernel_only": True, "rows": N_ROWS, "launch_ms": launch_ms,
                               "ms_per_step": total_ms / args.steps}), flush=True)
         return
+    f32_total, f32_launch, _ = timed(_lib.MFM_DTYPE_F32, max(10, args.steps // 5))
 
-    # e2e through the C ABI with pinned host buffers in the boundary format
+    # e2e through the C ABI with pinned host buffers in the boundary format:
+    # the model handle (parameters resident, uploaded once) and the
+    # reference-shaped stateless call (parameters uploaded every call)
+    from modern_fm_b200.model import DeviceModel
+
     Xh, keep = host_inputs(X)
-    w_h = w64.cpu().pin_memory()
-    V_h = V64.cpu().pin_memory()
+    w_h = w32.double().cpu().pin_memory()
+    V_h = V32.double().cpu().pin_memory()
     out_h = torch.empty(N_ROWS, dtype=torch.float64).pin_memory()
+    out_h2 = torch.empty(N_ROWS, dtype=torch.float64).pin_memory()
     csr, keep2 = _lib.make_csr(Xh.indptr, Xh.indices, Xh.data, N_FEATURES)
-    ex = _lib.Exec(_lib.MFM_DTYPE_F32, local, 1)
+    model = DeviceModel("fm", N_FEATURES, K, dtype="float32-float64", device=local)
+    model.set_params(w0, w_h.numpy(), V_h.numpy())
+    model_dtype = model.dtype_used
+    ex = _lib.Exec(_lib.MFM_DTYPE_F32_F64, local, 1)
 
     def e2e_step():
-        rc = L.mfm_fm_predict_csr(csr, w0, _lib.ptr(w_h.numpy()), _lib.ptr(V_h.numpy()), K,
-                                  _lib.ptr(out_h.numpy()), ex)
+        rc = L.mfm_model_predict_csr(model._h, csr, _lib.ptr(out_h.numpy()))
         if rc:
             raise RuntimeError(_lib.last_error())
 
-    for _ in range(2):
-        e2e_step()
+    def e2e_stateless():
+        rc = L.mfm_fm_predict_csr(csr, w0, _lib.ptr(w_h.numpy()), _lib.ptr(V_h.numpy()), K,
+                                  _lib.ptr(out_h2.numpy()), ex)
+        if rc:
+            raise RuntimeError(_lib.last_error())
+
+    def wall(fn, steps):
+        for _ in range(2):
+            fn()
+        barrier(world)
+        t = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        return max_over_ranks((time.perf_counter() - t) / steps, world)
+
     e2e_steps = max(2, min(args.steps, 5))
-    barrier(world)
-    t = time.perf_counter()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e2e_s = max_over_ranks((time.perf_counter() - t) / e2e_steps, world)
-    h2d = (Xh.indptr.nbytes + Xh.indices.nbytes + Xh.data.nbytes + w_h.numpy().nbytes
-           + V_h.numpy().nbytes)
+    e2e_s = wall(e2e_step, e2e_steps)
+    e2e_sl_s = wall(e2e_stateless, e2e_steps)
+    model.close()
+    h2d = Xh.indptr.nbytes + Xh.indices.nbytes + Xh.data.nbytes
+    h2d_sl = h2d + w_h.numpy().nbytes + V_h.numpy().nbytes
 
     # parity of the timed kernel's output on a row sample against the oracle
+    # (the same float32-valued parameters, float64 arithmetic): 1e-10
     from oracle import oracle as O
 
     samp = Xh.rows(0, 4000)
     want = O.fm_predict_fast_csr(samp.indptr, samp.indices, samp.data, N_FEATURES, w0,
                                  w_h.numpy(), V_h.numpy(), n_threads=8)
-    got = out[:4000].double().cpu().numpy()
-    parity = bool(np.all(np.abs(got - want) <= 1e-5 * np.abs(want) + 1e-5))
-    e2e_par = bool(np.allclose(out_h.numpy()[:4000], want, rtol=1e-5, atol=1e-5))
+    got = out[:4000].cpu().numpy()
+    parity = bool(np.allclose(got, want, rtol=1e-10, atol=1e-10))
+    e2e_par = bool(np.allclose(out_h.numpy()[:4000], want, rtol=1e-10, atol=1e-10)
+                   and np.allclose(out_h2.numpy()[:4000], want, rtol=1e-10, atol=1e-10))
+    got32 = out32[:4000].double().cpu().numpy()
+    par32 = bool(np.all(np.abs(got32 - want) <= 1e-5 * np.abs(want) + 1e-5))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -666,9 +780,9 @@ def run_ours(args):
         n_s = 300_000
         rate, _ = cpu_baseline(Xh, w0, w_h.numpy(), V_h.numpy(), n_s, threads)
         cpu = {"value": rate, "unit": "rows/s", "cores": threads, "kind": "port",
-               "sample": f"first {n_s} rows of the rank-0 test batch, rows split over "
-                         f"{threads} host threads (the reference's own CPU predict is "
-                         "single-threaded, rust/src/fm.rs:58-70)"}
+               "sample": f"first {n_s} rows of the rank-0 test batch, float64 arithmetic, rows "
+                         f"split over {threads} host threads (the reference's own CPU predict "
+                         "is single-threaded, rust/src/fm.rs:58-70)"}
 
     prep = None if args.no_prep else prep_measure(args, local, dev_t, L, _lib, X)
     libffm = (libffm_measure(local, dev_t)
@@ -684,20 +798,39 @@ def run_ours(args):
         peak, peak_kind = peaks()
         achieved = BYTES_PER_ROW * N_ROWS / (launch_ms / 1e3) / 1e9
         traffic = ncu_traffic()
+        f32_ms = f32_total / max(10, args.steps // 5)
+        a32 = BYTES_PER_ROW_F32 * N_ROWS / (f32_launch / 1e3) / 1e9
         line = {
             "metric": "FM CSR predict rows/s (CTR-shaped 39 fields, 2^22 features, k=16)",
             "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "param_storage": "f32",
+            "arithmetic": "float64 values, sums and scores on float32 parameters: the "
+                          "reference's computation for its default float32 estimator "
+                          "(python/modern_fm/fm.py:655-658, _backend.py:36-41)",
             "data": "synthetic (seeded, generated on the GPU)", "config": CONFIG,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": traffic, "bytes_per_row": BYTES_PER_ROW},
             "e2e": {"value": rows_total / e2e_s, "unit": "rows/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": N_ROWS * 8, "parity": e2e_par},
+                    "d2h_bytes_per_step": N_ROWS * 8, "parity": e2e_par,
+                    "path": "mfm_model_predict_csr (parameters resident in a model handle, "
+                            f"{model_dtype}); host CSR int64 / float64 up, float64 scores down",
+                    "stateless": {"value": rows_total / e2e_sl_s, "unit": "rows/s",
+                                  "h2d_bytes_per_step": h2d_sl,
+                                  "path": "mfm_fm_predict_csr (float64 parameters uploaded "
+                                          "every call, as the reference's CUDA predict)"}},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "parity": parity,
+            "parity_tolerance": "rtol = atol = 1e-10 against the oracle on 4,000 rows",
+            "f32": {"value": rows_total / (f32_ms / 1e3), "unit": "rows/s", "ms_per_step": f32_ms,
+                    "dtype": "f32", "parity": par32,
+                    "roofline": {"achieved": a32, "frac": a32 / peak,
+                                 "bytes_per_row": BYTES_PER_ROW_F32},
+                    "note": "float32 arithmetic throughout (secondary: narrower than the "
+                            "reference's float64)"},
         }
         if cpu:
             line["cpu_baseline"] = cpu

@@ -31,7 +31,20 @@ extern "C" {
 #define MFM_ERR_NO_DEVICE 2      /* no usable CUDA device */
 #define MFM_ERR_DEVICE_CHECK 3   /* a kernel's own bounds / status check fired */
 
-enum { MFM_DTYPE_F64 = 0, MFM_DTYPE_F32 = 1 };
+/* Compute types. MFM_DTYPE_F64: float64 parameters, values, arithmetic and
+ * scores (the reference's own arithmetic, rust/src/lib.rs:1-7). MFM_DTYPE_F32:
+ * float32 throughout (half the bytes of every gather). MFM_DTYPE_F32_F64:
+ * float32 parameters, float64 values, arithmetic and scores — what the
+ * reference computes for an estimator whose learned attributes are float32
+ * (its default, python/modern_fm/fm.py:655-658: the attributes are widened to
+ * float64 before its float64 kernels). Where parameters arrive as float64
+ * host arrays, F32_F64 stores them as float32 only when every value is exactly
+ * a float32 (checked on the device) and otherwise keeps float64, so its
+ * result is always the float64 arithmetic on the caller's values. Training
+ * keeps float64 parameters for the whole fit in F32_F64, as the reference
+ * does (python/modern_fm/_backend.py:116-130). */
+enum { MFM_DTYPE_F64 = 0, MFM_DTYPE_F32 = 1, MFM_DTYPE_F32_F64 = 2 };
+enum { MFM_MODEL_FM = 0, MFM_MODEL_FFM = 1, MFM_MODEL_FWFM = 2 };
 enum { MFM_LOSS_LOGISTIC = 0, MFM_LOSS_SQUARED = 1 };
 enum { MFM_OPT_SGD = 0, MFM_OPT_ADAGRAD = 1, MFM_OPT_ADAM = 2, MFM_OPT_FTRL = 3 };
 
@@ -46,9 +59,8 @@ typedef struct {
     int64_t n_features;
 } mfm_csr;
 
-/* Execution options. dtype selects the device arithmetic type of parameters,
- * sums and optimizer state (float64 reproduces the reference's float64
- * arithmetic; float32 halves the bytes every gather moves). device is the
+/* Execution options. dtype (MFM_DTYPE_*) selects the device storage and
+ * arithmetic types of parameters, sums and optimizer state. device is the
  * first CUDA ordinal; predict shards rows over n_devices devices. */
 typedef struct {
     int dtype;
@@ -170,7 +182,8 @@ int mfm_fwfm_fit_multiclass_csr(const mfm_csr* x, const int64_t* y,
 /* ---- device-resident prediction (no reference counterpart) -------------
  * Every pointer is DEVICE memory on `device`, already in the compute layout:
  * indptr int64 (n_rows+1), indices int32, data/w/v/r/out in `dtype`
- * (float or double). `stream` is a cudaStream_t (NULL = legacy default).
+ * (MFM_DTYPE_F32: all float; MFM_DTYPE_F64: all double; MFM_DTYPE_F32_F64:
+ * w/v/r float, data and out double). `stream` is a cudaStream_t (NULL = legacy default).
  * No host<->device copies, no allocation, no validation beyond sizes: the
  * caller guarantees the CSR is canonical and in range. Used for
  * device-resident throughput and by callers that keep data on the GPU. */
@@ -198,7 +211,8 @@ int mfm_fwfm_predict_device(int dtype, int device, const int64_t* indptr,
  * allowed. Output (caller-owned DEVICE buffers of n_rows+1 / nnz / nnz
  * entries): the canonical CSR in the compute layout the *_device entry points
  * take: columns sorted within each row, duplicates summed in float64 in their
- * original order (explicit zeros kept), indices int32, data in `dtype`.
+ * original order (explicit zeros kept), indices int32, data in `dtype`
+ * (float64 for MFM_DTYPE_F32_F64).
  * *nnz_out (host) receives the canonical entry count. Invalid CSR structure or
  * a column outside [0, n_features) returns MFM_ERR_INVALID with the
  * reference's message. Runs on `stream` (a cudaStream_t) and synchronises it. */
@@ -244,6 +258,58 @@ int mfm_fm_eval_device(int dtype, int device, const int64_t* indptr, const int32
                        int64_t k, const double* y, const double* sample_weight, int loss,
                        double label_smoothing, double* loss_out, void* stream);
 
+/* The same evaluation for the FFM and FwFM estimators' early-stopped fits,
+ * which score the validation set with ffm_predict / fwfm_predict on the host
+ * every epoch (python/modern_fm/ffm.py:210-212, python/modern_fm/fwfm.py:157-161).
+ * Parameters and field ids as in mfm_ffm_predict_device /
+ * mfm_fwfm_predict_device. */
+int mfm_ffm_eval_device(int dtype, int device, const int64_t* indptr, const int32_t* indices,
+                        const void* data, int64_t n_rows, const int32_t* field_ids,
+                        int64_t n_fields, double w0, const void* w, const void* v, int64_t k,
+                        const double* y, const double* sample_weight, int loss,
+                        double label_smoothing, double* loss_out, void* stream);
+int mfm_fwfm_eval_device(int dtype, int device, const int64_t* indptr, const int32_t* indices,
+                         const void* data, int64_t n_rows, const int32_t* field_ids,
+                         int64_t n_fields, double w0, const void* w, const void* v,
+                         const void* r, int64_t k, const double* y,
+                         const double* sample_weight, int loss, double label_smoothing,
+                         double* loss_out, void* stream);
+
+/* ---- persistent model handle ----------------------------------------------
+ * The reference uploads the parameters on every CUDA predict call
+ * (rust/src/cuda/mod.rs:9-12, rust/src/cuda/fm.rs:61-109) and scores a
+ * multiclass model with one binary call per class, each re-uploading X
+ * (python/modern_fm/fm.py:666-674, `decision_function`). A handle keeps one
+ * model's parameters resident on `device` across calls and scores every class
+ * of a row in one pass.
+ *   mfm_model_create: kind MFM_MODEL_*, dtype MFM_DTYPE_*, n_fields (FFM /
+ *     FwFM), k, n_classes (1 = binary: one score per row; C >= 2: C logits per
+ *     row, each the binary score with class c's parameters).
+ *   mfm_model_set_params: parameters in the reference's boundary layout,
+ *     float64 host arrays: binary w0 (scalar), w (n), V (n, k) or FFM
+ *     (n, F, k), R (F, F); multiclass class-major w0 (C), w (C, n),
+ *     V (C, n, k) or FFM (C, n, F, k), R (C, F, F); field_ids int64 (n) for
+ *     FFM / FwFM (NULL for FM). Uploaded once (key-major on the device).
+ *   mfm_model_info: the compute type the handle scores in (F32_F64 falls back
+ *     to F64 when the parameters are not exactly float32).
+ *   mfm_model_predict_csr: host CSR in the boundary format, validated as
+ *     mfm_fm_predict_csr does; out (n_rows) or (n_rows, C) float64.
+ *   mfm_model_predict_device: DEVICE CSR in the compute layout (indptr int64,
+ *     indices int32, canonical and in range); data and out float32 for
+ *     MFM_DTYPE_F32, float64 otherwise; on `stream` (a cudaStream_t), no
+ *     allocation, no synchronisation.
+ *   mfm_model_free: releases the device copies. */
+typedef struct mfm_model mfm_model;
+int mfm_model_create(int kind, int dtype, int device, int64_t n_features, int64_t n_fields,
+                     int64_t k, int64_t n_classes, mfm_model** out);
+int mfm_model_set_params(mfm_model* m, const double* w0, const double* w, const double* v,
+                         const double* r, const int64_t* field_ids);
+int mfm_model_info(const mfm_model* m, int* dtype_used);
+int mfm_model_predict_csr(mfm_model* m, const mfm_csr* x, double* out);
+int mfm_model_predict_device(mfm_model* m, const int64_t* indptr, const int32_t* indices,
+                             const void* data, int64_t n_rows, void* out, void* stream);
+void mfm_model_free(mfm_model* m);
+
 /* ---- allocation-free FM scoring --------------------------------------------
  * No counterpart in the reference: an addition for callers that cannot let
  * the library allocate GPU memory, such as a host that owns the whole device
@@ -256,10 +322,14 @@ int mfm_fm_eval_device(int dtype, int device, const int64_t* indptr, const int32
  * library holds until the process exits; no cudaMalloc, cudaFree or other
  * allocating routine is called. Inputs whose staging does not fit return
  * MFM_ERR_UNSUPPORTED before any device work. The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make that first
- * call before any stream capture. Calls share the array: each call clears the
- * flags it needs, and calls that overlap on the GPU race on the array (the
- * engine serialises calls on one device within a process). */
+ * loads the array's code module (the CUDA runtime loads modules lazily), which
+ * reserves the 64 MiB on that device, and looks up the array's device address
+ * (cudaGetSymbolAddress): make that first call before reserving the rest of
+ * the device for a pool, and before any stream capture. Calls run on the
+ * engine's own non-blocking stream for the device and synchronise it. Calls
+ * share the array: each call clears the flags it needs, and calls that overlap
+ * on the GPU race on the array (the engine serialises calls on one device
+ * within a process). MFM_DTYPE_F32_F64 computes as MFM_DTYPE_F64 here. */
 int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const double* w, const double* v,
                                int64_t k, double* out, const mfm_exec* ex);
 

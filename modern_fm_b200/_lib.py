@@ -15,7 +15,11 @@ LIB_PATH = os.path.join(PKG, "libmfm_b200.so")
 
 MFM_OK = 0
 MFM_ERR_INVALID, MFM_ERR_UNSUPPORTED = -1, -2
-MFM_DTYPE_F64, MFM_DTYPE_F32 = 0, 1
+MFM_DTYPE_F64, MFM_DTYPE_F32, MFM_DTYPE_F32_F64 = 0, 1, 2
+MFM_MODEL_FM, MFM_MODEL_FFM, MFM_MODEL_FWFM = 0, 1, 2
+DTYPES = {"float64": MFM_DTYPE_F64, "f64": MFM_DTYPE_F64, "float32": MFM_DTYPE_F32,
+          "f32": MFM_DTYPE_F32, "float32-float64": MFM_DTYPE_F32_F64,
+          "f32-f64": MFM_DTYPE_F32_F64, "f32_f64": MFM_DTYPE_F32_F64}
 LOSSES = {"logistic": 0, "squared": 1}
 OPTIMIZERS = {"sgd": 0, "adagrad": 1, "adam": 2, "ftrl": 3}
 
@@ -98,6 +102,24 @@ _SIGNATURES = {
                                       ct.c_int64, ct.c_double, ct.c_void_p, ct.c_void_p,
                                       ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_double,
                                       f64p, ct.c_void_p]),
+    "mfm_ffm_eval_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
+                                       ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_int64,
+                                       ct.c_double, ct.c_void_p, ct.c_void_p, ct.c_int64,
+                                       ct.c_void_p, ct.c_void_p, ct.c_int, ct.c_double, f64p,
+                                       ct.c_void_p]),
+    "mfm_fwfm_eval_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_void_p, ct.c_void_p,
+                                        ct.c_void_p, ct.c_int64, ct.c_void_p, ct.c_int64,
+                                        ct.c_double, ct.c_void_p, ct.c_void_p, ct.c_void_p,
+                                        ct.c_int64, ct.c_void_p, ct.c_void_p, ct.c_int,
+                                        ct.c_double, f64p, ct.c_void_p]),
+    "mfm_model_create": (ct.c_int, [ct.c_int, ct.c_int, ct.c_int, ct.c_int64, ct.c_int64,
+                                    ct.c_int64, ct.c_int64, ct.POINTER(ct.c_void_p)]),
+    "mfm_model_set_params": (ct.c_int, [ct.c_void_p, f64p, f64p, f64p, f64p, i64p]),
+    "mfm_model_info": (ct.c_int, [ct.c_void_p, ct.POINTER(ct.c_int)]),
+    "mfm_model_predict_csr": (ct.c_int, [ct.c_void_p, ct.POINTER(Csr), f64p]),
+    "mfm_model_predict_device": (ct.c_int, [ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p,
+                                            ct.c_int64, ct.c_void_p, ct.c_void_p]),
+    "mfm_model_free": (None, [ct.c_void_p]),
     "mfm_libffm_read": (ct.c_int, [ct.c_char_p, ct.c_int, ct.POINTER(ct.c_void_p)]),
     "mfm_libffm_info": (ct.c_int, [ct.c_void_p, i64p, i64p, i64p]),
     "mfm_libffm_arrays": (ct.c_int, [ct.c_void_p] + [ct.POINTER(ct.c_void_p)] * 5),
@@ -161,15 +183,27 @@ def make_csr(indptr, indices, data, n_features, exc=ValueError):
     return c, (indptr, indices, data)
 
 
+def dtype_code(dt):
+    """MFM_DTYPE_* code of a compute-type name (float64, float32,
+    float32-float64) or code."""
+    if isinstance(dt, int):
+        if dt in (MFM_DTYPE_F64, MFM_DTYPE_F32, MFM_DTYPE_F32_F64):
+            return dt
+    else:
+        code = DTYPES.get(str(dt))
+        if code is not None:
+            return code
+    raise ValueError(
+        f"unknown compute dtype {dt!r} (expected float64, float32 or float32-float64)")
+
+
 def exec_options(dtype=None, device=None, n_devices=None):
     """Execution options from arguments or the environment:
-    MFM_B200_DTYPE (float64 | float32, default float64), MFM_B200_DEVICE
-    (default 0), MFM_B200_NUM_GPUS (default 1)."""
-    dt = dtype or os.environ.get("MFM_B200_DTYPE", "float64")
-    code = {"float64": MFM_DTYPE_F64, "f64": MFM_DTYPE_F64, "float32": MFM_DTYPE_F32,
-            "f32": MFM_DTYPE_F32}.get(str(dt))
-    if code is None:
-        raise ValueError(f"unknown compute dtype {dt!r} (expected float64 or float32)")
+    MFM_B200_DTYPE (float32-float64 | float64 | float32, default
+    float32-float64: float64 arithmetic, parameters stored as float32 whenever
+    every value is exactly a float32), MFM_B200_DEVICE (default 0),
+    MFM_B200_NUM_GPUS (default 1)."""
+    code = dtype_code(dtype or os.environ.get("MFM_B200_DTYPE", "float32-float64"))
     dev = int(device if device is not None else os.environ.get("MFM_B200_DEVICE", "0"))
     nd = int(n_devices if n_devices is not None else os.environ.get("MFM_B200_NUM_GPUS", "1"))
     return Exec(code, dev, max(1, nd))

@@ -15,7 +15,7 @@ CPU-engine entry points of the reference (use_cuda=False and the
 *_predict_fast_* / *_predict_{csr,dense} functions) are not part of this
 engine: `modern_fm_b200.dropin` composes this module with a CPU backend.
 
-Compute dtype / devices come from MFM_B200_DTYPE (float64 default: the
+Compute dtype / devices come from MFM_B200_DTYPE (default float32-float64: the
 reference's own arithmetic), MFM_B200_DEVICE and MFM_B200_NUM_GPUS.
 """
 

@@ -441,9 +441,10 @@ extern "C" int mfm_csr_prep_device(int dtype, int device, int64_t n_rows, int64_
         if (n_features > INT32_MAX)
             fail(MFM_ERR_UNSUPPORTED, fmt("n_features %lld exceeds the engine's 2^31-1 limit",
                                           (long long)n_features));
-        if (dtype != MFM_DTYPE_F32 && dtype != MFM_DTYPE_F64)
+        if (dtype != MFM_DTYPE_F32 && dtype != MFM_DTYPE_F64 && dtype != MFM_DTYPE_F32_F64)
             fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
         DeviceGuard g(device);
+        // values keep float64 in both float64-arithmetic types
         cudaStream_t s = (cudaStream_t)stream;
         *nnz_out = dtype == MFM_DTYPE_F32
                        ? csr_prep<float>(device, s, n_rows, n_features, nnz, indptr, indices,

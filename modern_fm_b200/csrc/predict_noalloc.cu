@@ -10,11 +10,19 @@
 // kNoAllocScratchBytes (64 MiB) instead of allocating. Inputs that do not fit
 // are rejected with MFM_ERR_UNSUPPORTED before any device work.
 //
-// The array is part of this library's device image: every GPU that loads the
-// library holds it until the process exits. All calls share it and it keeps
-// the previous call's contents; the validation flags are cleared at the start
-// of every call. Calls are serialised per device by the engine's device lock;
+// The array is part of this file's device code module, which the CUDA runtime
+// loads lazily (CUDA 12 loads modules on first use): the first call on each
+// device loads it and so reserves the 64 MiB there, and every GPU that has
+// made a call holds it until the process exits. A caller that reserves the
+// rest of the device for its own pool makes its first call (any valid input)
+// before reserving the pool, and before any stream capture. All calls share
+// the array and it keeps the previous call's contents; the validation flags are
+// cleared at the start of every call. Calls are serialised per device by the
+// engine's device lock and run on the engine's stream for that device;
 // calls that overlapped on the GPU would race on the shared array.
+//
+// MFM_DTYPE_F32_F64 scores with the float64 parameters it stages: the same
+// float64 arithmetic on the caller's values.
 #include "common.cuh"
 
 namespace mfm {
@@ -84,7 +92,7 @@ extern "C" int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const dou
                  fmt("CUDA FM prediction supports 1 <= k <= 1024, got %lld", (long long)k));
         const int dtype = ex ? ex->dtype : MFM_DTYPE_F64;
         const int device = ex ? ex->device : 0;
-        if (dtype != MFM_DTYPE_F64 && dtype != MFM_DTYPE_F32)
+        if (dtype != MFM_DTYPE_F64 && dtype != MFM_DTYPE_F32 && dtype != MFM_DTYPE_F32_F64)
             fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
         const int64_t n = x->n_rows, nnz = x->nnz, nf = x->n_features;
         size_t need = region(sizeof(unsigned int)) + region((n + 1) * 8) + 2 * region(nnz * 8) +
@@ -97,7 +105,9 @@ extern "C" int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const dou
                      need, kNoAllocScratchBytes));
         DeviceGuard guard(device);
         std::lock_guard<std::mutex> lk(device_mutex(device));
-        cudaStream_t s = 0;  // legacy default stream: nothing is created either
+        // the engine's non-blocking stream for this device (created by the
+        // engine's first call on the device; no device memory is allocated)
+        cudaStream_t s = device_stream(device);
         Carve c{scratch_address(device)};
         unsigned int* flags = c.take<unsigned int>(1);
         int64_t* d_indptr = c.take<int64_t>(n + 1);
@@ -123,7 +133,7 @@ extern "C" int mfm_fm_predict_csr_noalloc(const mfm_csr* x, double w0, const dou
         if (h & 1u) fail(MFM_ERR_INVALID, "indptr must be non-decreasing");
         if (h & 2u)
             fail(MFM_ERR_INVALID, fmt("column index out of range [0, %lld)", (long long)nf));
-        if (dtype == MFM_DTYPE_F64) {
+        if (dtype != MFM_DTYPE_F32) {
             fm_launch_staged_f64(device, s, d_indptr, d_indices, d_data, n, w0, d_w, d_v, (int)k,
                                  d_out);
         } else {

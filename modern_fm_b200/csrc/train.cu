@@ -30,6 +30,7 @@
 #include <algorithm>
 #include <chrono>
 #include <thread>
+#include <cstdlib>
 #include <cstring>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -865,6 +866,15 @@ struct Trainer {
         EA.B = B;
         EA.n_rows = n_rows;
         EA.bar = bar.ptr;
+        // MFM_B200_EPOCH_SPIN_LIMIT: polls (~100 ns each) before a barrier wait
+        // gives up; MFM_B200_EPOCH_DROP_BLOCK: a block index that leaves at its
+        // first barrier without arriving (failure-handling tests only)
+        const char* sl = getenv("MFM_B200_EPOCH_SPIN_LIMIT");
+        EA.spin_limit = sl && *sl ? strtoull(sl, nullptr, 10) : kBarrierSpinLimit;
+        if (EA.spin_limit < 1 || EA.spin_limit > kBarrierSpinLimit)
+            EA.spin_limit = kBarrierSpinLimit;
+        const char* db = getenv("MFM_B200_EPOCH_DROP_BLOCK");
+        EA.drop_block = db && *db ? atoi(db) : -1;
         MFM_CUDA(cudaMemsetAsync(bar.ptr, 0, sizeof(GridBar), s), "barrier init");
         void* args[] = {&EA, &lgc};
         MFM_CUDA(cudaLaunchCooperativeKernel((const void*)kern, dim3(per_sm * sm_count(device)),
@@ -875,7 +885,8 @@ struct Trainer {
         MFM_CUDA(cudaStreamSynchronize(s), "epoch kernel");
         if (h.err)
             fail(MFM_ERR_DEVICE_CHECK,
-                 "a grid barrier wait gave up (blocks were not co-resident); results invalid");
+                 "a grid barrier wait gave up (a block did not arrive); the epoch stopped at "
+                 "that barrier and the parameters are invalid");
     }
 
     // true when the whole epoch ran as one persistent launch
@@ -1247,7 +1258,9 @@ void fit_dispatch(const FitSpec& f, const mfm_exec* ex) {
     validate_fit(f);
     const int dtype = ex ? ex->dtype : MFM_DTYPE_F64;
     const int device = ex ? ex->device : 0;
-    if (dtype == MFM_DTYPE_F64)
+    // float32 parameters with float64 arithmetic train as the reference does:
+    // float64 parameters and state for the whole fit (_backend.py:116-130)
+    if (dtype == MFM_DTYPE_F64 || dtype == MFM_DTYPE_F32_F64)
         fit_impl<double>(f, device);
     else if (dtype == MFM_DTYPE_F32)
         fit_impl<float>(f, device);
@@ -1401,6 +1414,10 @@ void fit_device_dispatch(int dtype, int device, const int64_t* indptr, const int
         fm_fit_device_impl<double>(device, s, indptr, indices, (const double*)data, n_rows,
                                    n_features, (const double*)y, (const double*)sample_weight,
                                    row_orders, tr, k, w0, w, v, dp);
+    else if (dtype == MFM_DTYPE_F32_F64)
+        fail(MFM_ERR_INVALID,
+             "device-resident training takes float64 (MFM_DTYPE_F64) or float32 arrays; "
+             "float32 parameters with float64 arithmetic train in float64");
     else
         fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
 }

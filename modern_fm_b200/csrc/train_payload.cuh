@@ -237,9 +237,11 @@ __global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t 
 // FM training runs a whole epoch's batch loop in one cooperative launch (all
 // blocks co-resident): forward -> barrier -> stage 1 (+ w0 by block 0) ->
 // [barrier -> stage 2, when the batch has multi-item runs] -> barrier. The
-// grid barrier's wait is bounded: after kBarrierSpinLimit polls it records an
-// error and moves on, so the launch always ends and the host reports
-// MFM_ERR_DEVICE_CHECK instead of waiting forever.
+// grid barrier's wait is bounded: after `limit` polls a block records an error
+// flag; a block that sees the flag (while waiting, or after any barrier)
+// returns at once, so after the first timeout the whole launch ends within one
+// more wait and the host reports MFM_ERR_DEVICE_CHECK, with no further batch
+// applied.
 
 struct GridBar {
     unsigned int count, gen, err, pad;
@@ -252,30 +254,42 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
     return v;
 }
 
-__device__ __forceinline__ void grid_barrier(GridBar* bar, unsigned int& gen) {
+// Returns false when the barrier failed (a wait gave up, here or in another
+// block): the caller returns. `drop` makes this block leave without arriving
+// (a block lost before the barrier, for the failure-handling test).
+__device__ __forceinline__ bool grid_barrier(GridBar* bar, unsigned int& gen,
+                                             unsigned long long limit, bool drop) {
+    __shared__ unsigned int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        const unsigned int g = gen;
-        __threadfence();  // release this block's writes
-        const unsigned int arrived = atomicAdd(&bar->count, 1u);
-        if (arrived == gridDim.x - 1) {
-            atomicExch(&bar->count, 0u);
-            __threadfence();
-            atomicExch(&bar->gen, g + 1u);
-        } else {
-            unsigned long long polls = 0;
-            while (ld_acquire_gpu(&bar->gen) == g) {
-                if (++polls > kBarrierSpinLimit) {
-                    atomicOr(&bar->err, 1u);
-                    break;
+        unsigned int ok = 0;
+        if (!drop) {
+            const unsigned int g = gen;
+            __threadfence();  // release this block's writes
+            const unsigned int arrived = atomicAdd(&bar->count, 1u);
+            if (arrived == gridDim.x - 1) {
+                atomicExch(&bar->count, 0u);
+                __threadfence();
+                atomicExch(&bar->gen, g + 1u);
+            } else {
+                unsigned long long polls = 0;
+                while (ld_acquire_gpu(&bar->gen) == g) {
+                    if (ld_acquire_gpu(&bar->err)) break;  // another block gave up
+                    if (++polls > limit) {
+                        atomicOr(&bar->err, 1u);
+                        break;
+                    }
+                    __nanosleep(100);
                 }
-                __nanosleep(100);
             }
+            __threadfence();  // acquire the other blocks' writes
+            ok = ld_acquire_gpu(&bar->err) == 0u;
         }
-        __threadfence();  // acquire the other blocks' writes
+        s_ok = ok;
     }
     ++gen;
     __syncthreads();
+    return s_ok != 0u;
 }
 
 template <class T>
@@ -287,6 +301,8 @@ struct EpochArgs {
     const int64_t* blong;   // per-batch first multi-item run (nb + 1)
     int64_t nb, B, n_rows;
     GridBar* bar;
+    unsigned long long spin_limit;  // polls before a barrier wait gives up
+    int drop_block;                 // block that leaves at its first barrier (-1: none)
 };
 
 // FK = 0: row-group forward <L = P1, LR = P2, CAP = P3>; FK = 1: generic
@@ -298,6 +314,7 @@ __global__ void __launch_bounds__(256, 2) fm_epoch_kernel(EpochArgs<T> E, int lg
     T(*wsum)[32 * VEC] = reinterpret_cast<T(*)[32 * VEC]>(sm + 256);
     unsigned char* fwd_smem = reinterpret_cast<unsigned char*>(sm + 256 + 8 * 32 * VEC);
     unsigned int gen = 0;
+    const bool drop = (int)blockIdx.x == E.drop_block;
     const int64_t gtid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
     for (int64_t b = 0; b < E.nb; ++b) {
@@ -311,7 +328,7 @@ __global__ void __launch_bounds__(256, 2) fm_epoch_kernel(EpochArgs<T> E, int lg
             fm_forward_rows_dev<T, VEC, P1, P2, P3>(A, gtid / P2, nthreads / P2);
         else
             fm_forward_dev<T, P1>(A, lgc, fwd_smem, gtid >> 5, nthreads >> 5);
-        grid_barrier(E.bar, gen);
+        if (!grid_barrier(E.bar, gen, E.spin_limit, drop)) return;
         RedArgs<T> R = E.red;
         R.seg = A.seg1;
         R.item0 = E.bitem[b];
@@ -322,10 +339,10 @@ __global__ void __launch_bounds__(256, 2) fm_epoch_kernel(EpochArgs<T> E, int lg
         if (blockIdx.x == 0) w0_dev(R, sm);
         reduce_items_dev<T, VEC>(R, n_items, gtid >> 5, nthreads >> 5);
         if (nl > 0) {
-            grid_barrier(E.bar, gen);
+            if (!grid_barrier(E.bar, gen, E.spin_limit, drop)) return;
             reduce_runs_dev<T, VEC>(R, l0, nl, blockIdx.x, gridDim.x, wsum);
         }
-        grid_barrier(E.bar, gen);
+        if (!grid_barrier(E.bar, gen, E.spin_limit, drop)) return;
     }
 }
 

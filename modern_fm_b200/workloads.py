@@ -254,10 +254,11 @@ def _mix32(t):
 
 
 def ctr_fm_torch(n_rows, seed, device="cuda", n_numeric=13, n_cat=26, vocab=2**20,
-                 space=2**22, zipf_s=1.1, head=4096):
+                 space=2**22, zipf_s=1.1, head=4096, value_dtype=None):
     """The ctr_fm workload drawn on the GPU (same distributions as `ctr_fm`,
     different random stream). Returns a dict of device tensors:
-    indptr int64 (n+1), indices int32 (nnz), data float32 (nnz), n_features.
+    indptr int64 (n+1), indices int32 (nnz), data (nnz) in `value_dtype`
+    (default float32; the values are drawn in float64), n_features.
     Rows are canonical: sorted, duplicate-free (a rare in-row hash collision
     is moved to the next free id)."""
     import torch
@@ -295,4 +296,5 @@ def ctr_fm_torch(n_rows, seed, device="cuda", n_numeric=13, n_cat=26, vocab=2**2
     z = n_numeric + n_cat
     indptr = torch.arange(0, n * z + 1, z, device=device, dtype=torch.int64)
     return dict(indptr=indptr, indices=idx.reshape(-1).to(torch.int32).contiguous(),
-                data=val.reshape(-1).to(torch.float32).contiguous(), n_features=space)
+                data=val.reshape(-1).to(value_dtype or torch.float32).contiguous(),
+                n_features=space)

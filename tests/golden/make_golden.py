@@ -364,11 +364,14 @@ MAKERS = ("predict", "train_binary", "train_multiclass", "prep", "losses", "libf
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference/python",
-                    help="path to the reference's python/ directory")
+    ap.add_argument("--reference", default=os.environ.get("MFM_REFERENCE_PYTHON"),
+                    help="path to the reference's python/ directory (default: "
+                         "$MFM_REFERENCE_PYTHON)")
     ap.add_argument("--only", nargs="*", choices=MAKERS, default=list(MAKERS),
                     help="fixture files to (re)generate")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set MFM_REFERENCE_PYTHON")
     sys.path.insert(0, args.reference)
     from modern_fm import _backend as B  # noqa: E402
     from modern_fm import _reference as R  # noqa: E402

@@ -1,7 +1,7 @@
 """The engine composed beneath the reference's unchanged Python package.
 
-Runs where the reference's python/ tree is available (set MFM_REFERENCE_PYTHON
-or keep the default location); elsewhere it is skipped. CPU only: the CPU
+Runs where the reference's python/ tree is available: set MFM_REFERENCE_PYTHON
+to that directory; without it the tests that need the package are skipped. CPU only: the CPU
 entry points are served by the C oracle standing in for the reference's Rust
 engine, and the CUDA entry points report no device here.
 """
@@ -16,7 +16,7 @@ import pytest
 from modern_fm_b200 import dropin
 from oracle import oracle as O
 
-REF = os.environ.get("MFM_REFERENCE_PYTHON", "/root/reference/python")
+REF = os.environ.get("MFM_REFERENCE_PYTHON", "")
 
 
 def test_composed_module_has_the_reference_surface():
@@ -32,8 +32,8 @@ def test_composed_module_has_the_reference_surface():
 
 @pytest.fixture
 def reference_pkg():
-    if not os.path.isdir(os.path.join(REF, "modern_fm")):
-        pytest.skip("reference python package not available")
+    if not REF or not os.path.isdir(os.path.join(REF, "modern_fm")):
+        pytest.skip("reference python package not available (set MFM_REFERENCE_PYTHON)")
     saved = {k: v for k, v in sys.modules.items() if k == "modern_fm" or k.startswith("modern_fm.")}
     for k in saved:
         del sys.modules[k]

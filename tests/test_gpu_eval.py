@@ -1,6 +1,8 @@
-"""GPU parity of the device early-stopping evaluation (mfm_fm_eval_device)
+"""GPU parity of the device early-stopping evaluation (mfm_{fm,ffm,fwfm}_eval_device)
 against the oracle: the reference's `metric(y_val, fm_predict_fast(X_val,
-...))` (python/modern_fm/fm.py:321-322) restated on the CPU.
+...))` (python/modern_fm/fm.py:321-322), and its FFM / FwFM counterparts
+(python/modern_fm/ffm.py:210-212, python/modern_fm/fwfm.py:157-161), restated
+on the CPU.
 
 Tolerances: float64 compute 1e-9 relative (scores within the reference's CUDA
 bar of 1e-10, the mean in another addition order); float32 compute 1e-4
@@ -37,9 +39,10 @@ def _run(case, dtype, loss, eps, weighted):
 
     ip, ix, dv, w0, w, V, y, sw = case
     tdt = torch.float32 if dtype == "float32" else torch.float64
+    pdt = torch.float64 if dtype == "float64" else torch.float32
     c = lambda a, t: torch.from_numpy(np.ascontiguousarray(a)).to("cuda", t)  # noqa: E731
-    return fm_eval_device(c(ip, torch.int64), c(ix, torch.int32), c(dv, tdt), w0, c(w, tdt),
-                          c(V, tdt), c(y, torch.float64),
+    return fm_eval_device(c(ip, torch.int64), c(ix, torch.int32), c(dv, tdt), w0, c(w, pdt),
+                          c(V, pdt), c(y, torch.float64),
                           c(sw, torch.float64) if weighted else None, loss=loss,
                           label_smoothing=eps)
 
@@ -52,13 +55,18 @@ def _want(case, loss, eps, weighted):
     return O.squared_loss(y, s, sample_weight=sw if weighted else None)
 
 
-@pytest.mark.parametrize("dtype,rtol", [("float64", 1e-9), ("float32", 1e-4)])
+@pytest.mark.parametrize("dtype,rtol", [("float64", 1e-9), ("float32", 1e-4),
+                                        ("float32-float64", 1e-9)])
 @pytest.mark.parametrize("loss,eps,weighted", [("logistic", 0.0, False),
                                                ("logistic", 0.1, True),
                                                ("squared", 0.0, False),
                                                ("squared", 0.0, True)])
 def test_eval_matches_oracle(dtype, rtol, loss, eps, weighted):
     case = _case(1)
+    if dtype == "float32-float64":  # float32 parameters, float64 values and arithmetic
+        ip, ix, dv, w0, w, V, y, sw = case
+        case = (ip, ix, dv, w0, w.astype(np.float32).astype(np.float64),
+                V.astype(np.float32).astype(np.float64), y, sw)
     got = _run(case, dtype, loss, eps, weighted)
     want = _want(case, loss, eps, weighted)
     assert got == pytest.approx(want, rel=rtol)
@@ -94,3 +102,44 @@ def test_device_eval_matches_reference_golden(case, dtype, rtol):
          np.zeros((n, k)), case.a["y"], case.a["sample_weight"])
     got = _run(c, dtype, case["loss"], case["label_smoothing"], case["weighted"])
     assert got == pytest.approx(case.a["value"][0], rel=rtol)
+
+
+@pytest.mark.parametrize("model", ["ffm", "fwfm"])
+@pytest.mark.parametrize("dtype,rtol", [("float64", 1e-9), ("float32", 1e-4),
+                                        ("float32-float64", 1e-9)])
+@pytest.mark.parametrize("loss,eps,weighted", [("logistic", 0.1, True), ("squared", 0.0, False)])
+def test_field_aware_eval_matches_oracle(model, dtype, rtol, loss, eps, weighted):
+    from modern_fm_b200.evaluate import ffm_eval_device, fwfm_eval_device
+
+    rng = np.random.default_rng(17)
+    n, d, F, k = 3000, 600, 6, 4
+    X = sp.random(n, d, density=0.01, format="csr", random_state=17,
+                  data_rvs=lambda m: rng.lognormal(0.0, 0.5, size=m))
+    ip, ix, dv = X.indptr.astype(np.int64), X.indices.astype(np.int64), X.data
+    fid = rng.integers(0, F, size=d)
+    w0, w = 0.1, rng.normal(size=d) * 0.3
+    V = rng.normal(size=(d, F, k) if model == "ffm" else (d, k)) * 0.3
+    R = rng.uniform(size=(F, F))
+    if dtype != "float64":
+        w, V, R = (a.astype(np.float32).astype(np.float64) for a in (w, V, R))
+    y = (rng.random(n) < 0.3).astype(np.float64)
+    sw = rng.uniform(0.5, 2.0, size=n)
+    if model == "ffm":
+        s = O.ffm_predict_csr(ip, ix, dv, d, fid, w0, w, V)
+    else:
+        s = O.fwfm_predict_csr(ip, ix, dv, d, fid, w0, w, V, R)
+    swa = sw if weighted else None
+    want = (O.logistic_loss(y, s, label_smoothing=eps, sample_weight=swa) if loss == "logistic"
+            else O.squared_loss(y, s, sample_weight=swa))
+    tdt = torch.float32 if dtype == "float32" else torch.float64
+    pdt = torch.float64 if dtype == "float64" else torch.float32
+    c = lambda a, t: torch.from_numpy(np.ascontiguousarray(a)).to("cuda", t)  # noqa: E731
+    args = (c(ip, torch.int64), c(ix, torch.int32), c(dv, tdt), c(fid, torch.int32), w0,
+            c(w, pdt), c(V, pdt))
+    kw = dict(sample_weight=c(sw, torch.float64) if weighted else None, loss=loss,
+              label_smoothing=eps)
+    if model == "ffm":
+        got = ffm_eval_device(*args, c(y, torch.float64), **kw)
+    else:
+        got = fwfm_eval_device(*args, c(R, pdt), c(y, torch.float64), **kw)
+    assert got == pytest.approx(want, rel=rtol)

@@ -1,10 +1,12 @@
 """GPU parity of the CSR scoring kernels (FM / FFM / FwFM), through the C ABI,
 against the C oracle and the reference's NumPy golden outputs.
 
-Tolerances: float64 compute uses the reference's own CUDA bar, rtol = atol =
-1e-10 (tests/test_cuda_parity.py:30-31); float32 compute uses the target bar
-of 1e-5 relative, with an absolute floor of 1e-5 times the row's magnitude
-scale (sum of |terms|) so that scores near zero are judged on their scale.
+Tolerances: float64 arithmetic (MFM_DTYPE_F64, and MFM_DTYPE_F32_F64 on
+float32-valued parameters) uses the reference's own CUDA bar, rtol = atol =
+1e-10 (tests/test_cuda_parity.py:30-31); float32 arithmetic uses the target
+bar of 1e-5 relative, with an absolute floor of 1e-5 times the row's
+magnitude scale (the sum of the absolute values of the score's terms) so that
+scores near zero are judged on their scale.
 """
 
 import numpy as np
@@ -27,6 +29,36 @@ def f32(monkeypatch):
     monkeypatch.setenv("MFM_B200_DTYPE", "float32")
 
 
+@pytest.fixture
+def f64(monkeypatch):
+    monkeypatch.setenv("MFM_B200_DTYPE", "float64")
+
+
+def _abs_scale(case):
+    """Per-row sum of |terms| of the score: the oracle's score of the same
+    row with every value, parameter and weight replaced by its magnitude."""
+    a = case.a
+    n, m = case["n_features"], case["model"]
+    ip, ix, dv = a["indptr"], a["indices"], np.abs(a["data"])
+    if m == "fm":
+        return _scale_fm(ip, ix, a["data"], case["w0"], a["w"], a["V"])
+    if m == "ffm":
+        return O.ffm_predict_csr(ip, ix, dv, n, a["field_ids"], abs(case["w0"]),
+                                 np.abs(a["w"]), np.abs(a["V"])) + 1.0
+    return O.fwfm_predict_csr(ip, ix, dv, n, a["field_ids"], abs(case["w0"]), np.abs(a["w"]),
+                              np.abs(a["V"]), np.abs(a["r"])) + 1.0
+
+
+def _round32(case):
+    """The case with every parameter rounded to float32 (as a float32
+    estimator's attributes are), values kept float64."""
+    a = dict(case.a)
+    for key in ("w", "V", "r"):
+        if key in a:
+            a[key] = a[key].astype(np.float32).astype(np.float64)
+    return golden_io.Case(dict(case), a)
+
+
 def _scale_fm(ip, ix, dv, w0, w, V):
     """Per-row sum of the absolute terms of the FM score (for float32 atol)."""
     n = len(ip) - 1
@@ -43,7 +75,7 @@ def _random_csr(rng, n, d, density):
 
 
 @pytest.mark.parametrize("case", golden_io.load("predict.npz"), ids=lambda c: c.name)
-def test_predict_golden_f64(case):
+def test_predict_golden_f64(case, f64):
     got = run_cases.predict_case(_rust, case, cuda=True)
     np.testing.assert_allclose(got, case.a["out"], rtol=RTOL64, atol=ATOL64)
     np.testing.assert_allclose(got, run_cases.predict_case(O, case, cuda=False), rtol=RTOL64,
@@ -54,16 +86,37 @@ def test_predict_golden_f64(case):
 def test_predict_golden_f32(case, f32):
     got = run_cases.predict_case(_rust, case, cuda=True)
     want = case.a["out"]
-    a = case.a
-    if case["model"] == "fm":
-        scale = _scale_fm(a["indptr"], a["indices"], a["data"], case["w0"], a["w"], a["V"])
-    else:
-        scale = np.abs(want) + 10.0 * np.abs(a["V"]).max() ** 2 * 50
+    scale = _abs_scale(case)
     assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-5 * scale)
 
 
+@pytest.mark.parametrize("case", golden_io.load("predict.npz"), ids=lambda c: c.name)
+def test_predict_golden_f32_f64(case, monkeypatch):
+    """float32 parameters, float64 values and arithmetic: the reference's
+    computation for a float32 estimator. Against the oracle on the same
+    float32-rounded parameters at the float64 bar."""
+    monkeypatch.setenv("MFM_B200_DTYPE", "float32-float64")
+    c = _round32(case)
+    got = run_cases.predict_case(_rust, c, cuda=True)
+    want = run_cases.predict_case(O, c, cuda=False)
+    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=ATOL64)
+
+
+def test_f32_f64_inexact_parameters_fall_back_to_f64(monkeypatch):
+    """Parameters that are not float32 values are scored in float64: the
+    result is bitwise that of MFM_DTYPE_F64."""
+    rng = np.random.default_rng(11)
+    ip, ix, dv = _random_csr(rng, 500, 300, 0.05)
+    w0, w, V = 0.3, rng.normal(size=300), rng.normal(size=(300, 16)) * 0.2
+    monkeypatch.setenv("MFM_B200_DTYPE", "float64")
+    a = _rust.fm_predict_cuda_csr(ip, ix, dv, 300, w0, w, V)
+    monkeypatch.setenv("MFM_B200_DTYPE", "float32-float64")
+    b = _rust.fm_predict_cuda_csr(ip, ix, dv, 300, w0, w, V)
+    np.testing.assert_array_equal(a, b)
+
+
 @pytest.mark.parametrize("k", [1, 2, 3, 4, 8, 12, 16, 17, 24, 32, 64, 130, 1024])
-@pytest.mark.parametrize("dtype", ["float64", "float32"])
+@pytest.mark.parametrize("dtype", ["float64", "float32", "float32-float64"])
 def test_fm_predict_k_range(k, dtype, monkeypatch):
     """Every latent width reaches a kernel shape (row-group or generic); rows
     of 0 to 150 nonzeros cover one and several gather iterations."""
@@ -74,9 +127,11 @@ def test_fm_predict_k_range(k, dtype, monkeypatch):
     ip = np.concatenate([ip, ip2[1:] + ip[-1]])
     ix, dv = np.concatenate([ix, ix2]), np.concatenate([dv, dv2])
     w0, w, V = rng.normal(), rng.normal(size=200), rng.normal(size=(200, k)) * 0.3
+    if dtype == "float32-float64":
+        w, V = w.astype(np.float32).astype(np.float64), V.astype(np.float32).astype(np.float64)
     want = O.fm_predict_fast_csr(ip, ix, dv, 200, w0, w, V)
     got = _rust.fm_predict_cuda_csr(ip, ix, dv, 200, w0, w, V)
-    if dtype == "float64":
+    if dtype != "float32":
         np.testing.assert_allclose(got, want, rtol=RTOL64, atol=1e-9 * max(1.0, k / 16))
     else:
         scale = _scale_fm(ip, ix, dv, w0, w, V)
@@ -132,7 +187,7 @@ def test_known_answers():
     assert abs(out[0] - 9.5) < 1e-12
 
 
-def test_ffm_large_row():
+def test_ffm_large_row(f64):
     # a single row with z = 2048 nonzeros (tests/test_cuda_parity.py:126-136)
     rng = np.random.default_rng(0)
     d = 2048
@@ -166,6 +221,22 @@ def test_predict_validation_on_device():
     with pytest.raises(RuntimeError, match="1 <= k <= 1024"):
         _rust.fm_predict_cuda_csr(np.array([0, 1]), np.array([0]), np.ones(1), 2, 0.0,
                                   np.zeros(2), np.zeros((2, 1025)))
+
+
+def test_ctr_shaped_f32_f64_against_oracle(monkeypatch):
+    """The CTR-shaped FM workload (39 fields, Zipf ids, k=16) with float32
+    parameters and float64 arithmetic, at the float64 bar."""
+    from modern_fm_b200 import workloads
+
+    monkeypatch.setenv("MFM_B200_DTYPE", "float32-float64")
+    X, _ = workloads.ctr_fm(n_rows=20000, seed=6)
+    rng = np.random.default_rng(2)
+    d = X.n_features
+    w = rng.normal(0, 0.1, d).astype(np.float32).astype(np.float64)
+    V = rng.normal(0, 0.1, (d, 16)).astype(np.float32).astype(np.float64)
+    want = O.fm_predict_fast_csr(X.indptr, X.indices, X.data, d, -3.0, w, V, n_threads=4)
+    got = _rust.fm_predict_cuda_csr(X.indptr, X.indices, X.data, d, -3.0, w, V)
+    np.testing.assert_allclose(got, want, rtol=RTOL64, atol=ATOL64)
 
 
 def test_ctr_shaped_f32_against_oracle(f32):
