@@ -674,10 +674,15 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev_t)
 
     def step(dtype=_lib.MFM_DTYPE_F32_F64):
+        # each compute type with arrays of its own element types: float32 data /
+        # parameters / scores; float64 data with float32 parameters; float64
         src, o = (X32, out32) if dtype == _lib.MFM_DTYPE_F32 else (X, out)
+        pw, pv = (w64, V64) if dtype == _lib.MFM_DTYPE_F64 else (w32, V32)
+        assert pv.element_size() == (8 if dtype == _lib.MFM_DTYPE_F64 else 4)
+        assert src["data"].element_size() == (4 if dtype == _lib.MFM_DTYPE_F32 else 8)
         rc = L.mfm_fm_predict_device(dtype, local, src["indptr"].data_ptr(),
                                      src["indices"].data_ptr(), src["data"].data_ptr(), N_ROWS,
-                                     w0, w32.data_ptr(), V32.data_ptr(), K, o.data_ptr(),
+                                     w0, pw.data_ptr(), pv.data_ptr(), K, o.data_ptr(),
                                      stream.cuda_stream)
         if rc:
             raise RuntimeError(_lib.last_error())
@@ -709,12 +714,15 @@ def run_ours(args):
                                 world)
         return total, launch, clk.summary() if clocks else None
 
-    total_ms, launch_ms, clocks = timed(_lib.MFM_DTYPE_F32_F64, args.steps, clocks=True)
-    if args.kernel_only:
+    if args.kernel_only:  # profiling runs: one scoring kernel, no other measurement
+        kd = _lib.dtype_code(args.kernel_dtype)
+        total_ms, launch_ms, _ = timed(kd, args.steps)
         if rank == 0:
-            print(json.dumps({"kernel_only": True, "rows": N_ROWS, "launch_ms": launch_ms,
-                              "ms_per_step": total_ms / args.steps}), flush=True)
+            print(json.dumps({"kernel_only": True, "dtype": args.kernel_dtype, "rows": N_ROWS,
+                              "launch_ms": launch_ms, "ms_per_step": total_ms / args.steps}),
+                  flush=True)
         return
+    total_ms, launch_ms, clocks = timed(_lib.MFM_DTYPE_F32_F64, args.steps, clocks=True)
     f32_total, f32_launch, _ = timed(_lib.MFM_DTYPE_F32, max(10, args.steps // 5))
 
     # e2e through the C ABI with pinned host buffers in the boundary format:
@@ -910,8 +918,8 @@ def run_suite(args):
     rng = np.random.default_rng(0)
     lines = []
     if "c0" in args.suite or "c1" in args.suite:
-        Xtr, ytr, fid = WL.onehot_ctr(40000, 0)
-        Xte, _, _ = WL.onehot_ctr(20000, 100)
+        Xall, yall, fid = WL.onehot_ctr(60000, 0)  # one draw: 40k train / 20k test rows
+        Xtr, ytr, Xte = Xall.rows(0, 40000), yall[:40000], Xall.rows(40000, 60000)
         ro = WL.row_orders(Xtr.n_rows, 10, 1)
     if "c0" in args.suite:  # FM k=16, AdaGrad 0.05, batch 512, 10 epochs
         d, k = Xtr.n_features, 16
@@ -1012,6 +1020,9 @@ def main():
     ap.add_argument("--train-cpu-rows", type=int, default=200_000)
     ap.add_argument("--kernel-only", action="store_true",
                     help="time only the device-resident kernel (profiling runs)")
+    ap.add_argument("--kernel-dtype", default="float32-float64",
+                    choices=["float32-float64", "float32", "float64"],
+                    help="compute type of the --kernel-only scoring kernel")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--suite", default="",
                     help="comma list of the other configurations to time instead (c0,c1,c3,c4)")

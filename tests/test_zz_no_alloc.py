@@ -82,18 +82,22 @@ FIRST_CALL = r"""
 import sys, json, numpy as np, torch
 sys.path.insert(0, {root!r})
 torch.zeros(1, device="cuda")  # the CUDA context exists before the measurement
+import ctypes as ct
 from modern_fm_b200 import _lib
 L = _lib.lib()
+fn = L.mfm_fm_predict_csr_noalloc
+fn.restype = ct.c_int
+fn.argtypes = [ct.POINTER(_lib.Csr), ct.c_double, _lib.f64p, _lib.f64p, ct.c_int64, _lib.f64p,
+               ct.POINTER(_lib.Exec)]
+L.mfm_noalloc_scratch_bytes.restype = ct.c_int64
 ip, ix, dv = np.array([0, 2], np.int64), np.array([0, 3], np.int64), np.array([1.0, 2.0])
 w, V = np.ones(4), np.ones((4, 2))
 csr, keep = _lib.make_csr(ip, ix, dv, 4)
 out = np.zeros(1)
 free0 = torch.cuda.mem_get_info(0)[0]
-rc = L.mfm_fm_predict_csr_noalloc(csr, 0.5, _lib.ptr(w), _lib.ptr(V), 2, _lib.ptr(out),
-                                  _lib.Exec(0, 0, 1))
+rc = fn(csr, 0.5, _lib.ptr(w), _lib.ptr(V), 2, _lib.ptr(out), _lib.Exec(0, 0, 1))
 free1 = torch.cuda.mem_get_info(0)[0]
-rc2 = L.mfm_fm_predict_csr_noalloc(csr, 0.5, _lib.ptr(w), _lib.ptr(V), 2, _lib.ptr(out),
-                                   _lib.Exec(0, 0, 1))
+rc2 = fn(csr, 0.5, _lib.ptr(w), _lib.ptr(V), 2, _lib.ptr(out), _lib.Exec(0, 0, 1))
 free2 = torch.cuda.mem_get_info(0)[0]
 print(json.dumps(dict(rc=rc, rc2=rc2, first_drop=free0 - free1, second_drop=free1 - free2,
                       out=float(out[0]), scratch=int(L.mfm_noalloc_scratch_bytes()))))
