@@ -639,6 +639,246 @@ def libffm_measure(local, dev_t):
         return {"error": f"{type(exc).__name__}: {exc}"}
 
 
+def _device_rate(fn, steps, stream):
+    """Mean ms per call of `fn` (CUDA events on the launch stream, 3 warm-up
+    calls)."""
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def _roof(bytes_per_row, rows, ms):
+    peak, kind = peaks()
+    ach = bytes_per_row * rows / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+            "peak_kind": kind, "bytes_per_row": bytes_per_row}
+
+
+def _check(rc, _lib):
+    if rc:
+        raise RuntimeError(_lib.last_error())
+
+
+def configs_measure(args, local, dev_t, L, _lib):
+    """The other configurations, at N = 1, in the reference's arithmetic
+    (float32 parameters with float64 values and math for scoring, float64
+    training). Per configuration: device-resident scoring rows/s over a
+    2,000,000-row batch of its generator with the roofline of its algorithmic
+    bytes, parity of those scores against the oracle on a row sample (1e-10),
+    e2e scoring through the model handle (host CSR in, scores out), one fit
+    through the reference-facing C ABI (host float64 buffers, transfers
+    included) at the configuration's hyperparameters, and the oracle's fit and
+    scoring of a bounded sample on the host cores as cpu_baseline.
+      ffm      C1: FFM k=8, 16 one-hot fields x 16, AdaGrad 0.05, batch 512,
+               10 epochs over 40,000 rows;
+      fwfm     C3: FwFM k=8, 9 Zipf one-hot fields (~373k features), FTRL
+               (alpha 0.05, beta 1, l1 1.0 / 0.1), batch 1024, 1 epoch over
+               200,000 rows;
+      softmax  C4: softmax FM C=10, k=8, ragged Poisson(30)+1 rows over 1M
+               features, Adam 1e-3, batch 2048, sample weights, label
+               smoothing 0.1, 3 epochs over --softmax-rows rows."""
+    import torch
+
+    from modern_fm_b200 import _rust
+    from modern_fm_b200 import workloads as WL
+    from modern_fm_b200.model import DeviceModel
+    from oracle import oracle as O
+
+    os.environ["MFM_B200_DTYPE"] = "float32-float64"
+    stream = torch.cuda.current_stream(dev_t)
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    res = {}
+    T = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(dev_t, dt)  # noqa: E731
+
+    def r32(a):
+        return np.asarray(a, dtype=np.float32).astype(np.float64)
+
+    def scoring(kind, X, fid, F, k, w0, w, V, R, bytes_per_row, C=1):
+        """Device-resident scoring (model handle, float32-float64), parity,
+        e2e through the handle."""
+        n = X.n_rows
+        m = DeviceModel(kind, X.n_features, k, n_fields=F, n_classes=C, device=local)
+        m.set_params(w0, w, V, R, fid)
+        ip, ix, dv = T(X.indptr, torch.int64), T(X.indices, torch.int32), T(X.data, torch.float64)
+        out = torch.empty((n, C) if C > 1 else (n,), dtype=torch.float64, device=dev_t)
+        ms = _device_rate(lambda: m.predict_device(ip, ix, dv, out, stream), 10, stream)
+        samp = X.rows(0, 2000)
+        got = out[:2000].cpu().numpy().reshape(2000, C)
+        ok = True
+        for c in range(C):
+            pc = (lambda a: a[c]) if C > 1 else (lambda a: a)
+            if kind == "fm":
+                want = O.fm_predict_fast_csr(samp.indptr, samp.indices, samp.data, X.n_features,
+                                             pc(w0), pc(w), pc(V))
+            elif kind == "ffm":
+                want = O.ffm_predict_csr(samp.indptr, samp.indices, samp.data, X.n_features, fid,
+                                         pc(w0), pc(w), pc(V))
+            else:
+                want = O.fwfm_predict_csr(samp.indptr, samp.indices, samp.data, X.n_features,
+                                          fid, pc(w0), pc(w), pc(V), pc(R))
+            ok &= bool(np.allclose(got[:, c], want, rtol=1e-10, atol=1e-10))
+        hbuf = np.empty((n, C) if C > 1 else (n,))
+        m.predict_csr(X.indptr, X.indices, X.data, out=hbuf)
+        t = time.perf_counter()
+        for _ in range(3):
+            m.predict_csr(X.indptr, X.indices, X.data, out=hbuf)
+        e2e = (time.perf_counter() - t) / 3
+        mdt = m.dtype_used
+        m.close()
+        return {"rows": n, "rows_per_s": n / (ms / 1e3), "ms_per_launch": ms,
+                "dtype": "f64", "param_storage": "f32" if mdt == "float32-float64" else "f64",
+                "roofline": _roof(bytes_per_row, n, ms), "parity": ok,
+                "e2e": {"rows_per_s": n / e2e, "h2d_bytes_per_step": X.indptr.nbytes +
+                        X.indices.nbytes + X.data.nbytes, "d2h_bytes_per_step": hbuf.nbytes,
+                        "path": "mfm_model_predict_csr"}}
+
+    # ---- C1: FFM ----
+    try:
+        Xs, ys, fid = WL.onehot_ctr(2_000_000, 7)
+        Xall, yall, _ = WL.onehot_ctr(60000, 0)
+        Xtr, ytr, Xte = Xall.rows(0, 40000), yall[:40000], Xall.rows(40000, 60000)
+        d, F, k = 256, 16, 8
+        V0 = rng.uniform(0, 0.1, (d, F, k))
+        ro = WL.row_orders(Xtr.n_rows, 10, 1)
+
+        def fit(mod, cuda, epochs, n_jobs=1):
+            w, V = np.zeros(d), V0.copy()
+            r = mod.ffm_fit_csr(Xtr.indptr, Xtr.indices, Xtr.data, d, ytr, np.ones(Xtr.n_rows),
+                                fid, 0.0, 0.0, w, V, np.zeros(d), np.zeros_like(V), "logistic",
+                                "adagrad", 0.05, 1e-5, 1e-5, 0.9, 0.999, 1e-8, ro[:epochs], 512,
+                                n_jobs, 0.0, 0.0, 1.0, use_cuda=cuda)
+            return r[0], w, V
+        fit(_rust, True, 10)
+        t = time.perf_counter()
+        w0, w, V = fit(_rust, True, 10)
+        fit_s = time.perf_counter() - t
+        t = time.perf_counter()
+        fit(O, False, 1, threads)
+        cpu_fit = Xtr.n_rows / (time.perf_counter() - t)
+        t = time.perf_counter()
+        O.ffm_predict_csr(Xte.indptr, Xte.indices, Xte.data, d, fid, w0, w, V, n_threads=threads)
+        cpu_pred = Xte.n_rows / (time.perf_counter() - t)
+        # predict bytes per row (float32 parameters, float64 values and scores):
+        # indptr 8 + z (index 4 + value 8) + z w 4 + z (z-1) pair slots k 4 + score 8
+        z = 16
+        res["ffm"] = {
+            "workload": "C1: FFM k=8, 16 one-hot fields x 16 categories (256 features), "
+                        "field = feature // 16",
+            "predict": scoring("ffm", Xs, fid, F, k, w0, r32(w), r32(V), None,
+                               8 + z * 12 + z * 4 + z * (z - 1) * k * 4 + 8),
+            "train": {"fit_s": fit_s, "rows_per_s": Xtr.n_rows * 10 / fit_s, "dtype": "f64",
+                      "path": "mfm_ffm_fit_csr (host float64 buffers, transfers included)",
+                      "config": "AdaGrad 0.05, batch 512, 10 epochs, 40,000 rows"},
+            "cpu_baseline": {"value": cpu_fit, "unit": "train rows/s", "predict_rows_per_s":
+                             cpu_pred, "cores": threads, "kind": "port",
+                             "sample": "one epoch of the 40,000 training rows (n_jobs = every "
+                                       "host thread) and scoring of the 20,000 test rows"}}
+    except Exception as exc:
+        res["ffm"] = {"error": f"{type(exc).__name__}: {exc}"}
+
+    # ---- C3: FwFM FTRL ----
+    try:
+        X, y, fid = WL.fwfm_ctr(200000, 3)
+        Xs, _, _ = WL.fwfm_ctr(2_000_000, 13, labels=False)
+        d, F, k = X.n_features, 9, 8
+        V0 = rng.normal(0, 0.01, (d, k))
+        ro = WL.row_orders(X.n_rows, 1, 5)
+
+        def fitw(mod, cuda, Xf, yf, rof):
+            w, V, R = np.zeros(d), V0.copy(), np.ones((F, F))
+            r = mod.fwfm_fit_csr(Xf.indptr, Xf.indices, Xf.data, d, yf, np.ones(Xf.n_rows), fid,
+                                 0.0, 0.0, w, V, R, np.zeros(d), np.zeros((d, k)),
+                                 np.zeros((F, F)), "logistic", "ftrl", 0.05, 0.0, 0.0, 0.9,
+                                 0.999, 1e-8, rof, 1024, 1.0, 0.1, 1.0, use_cuda=cuda)
+            return r[0], w, V, R
+        fitw(_rust, True, X, y, ro)
+        t = time.perf_counter()
+        w0, w, V, R = fitw(_rust, True, X, y, ro)
+        fit_s = time.perf_counter() - t
+        n_c = 40000
+        Xc = X.rows(0, n_c)
+        t = time.perf_counter()
+        fitw(O, False, Xc, y[:n_c], np.arange(n_c)[None, :])
+        cpu_fit = n_c / (time.perf_counter() - t)
+        t = time.perf_counter()
+        O.fwfm_predict_csr(X.indptr, X.indices, X.data, d, fid, w0, w, V, R, n_threads=threads)
+        cpu_pred = X.n_rows / (time.perf_counter() - t)
+        z = 9  # indptr 8 + z (4 + 8) + z (k + 1) 4 (w, V) + score 8; R read from cache
+        res["fwfm"] = {
+            "workload": "C3: FwFM k=8, 9 one-hot Zipf(1.05) fields, ~373k features",
+            "predict": scoring("fwfm", Xs, fid, F, k, w0, r32(w), r32(V), r32(R),
+                               8 + z * 12 + z * (k + 1) * 4 + 8),
+            "train": {"fit_s": fit_s, "rows_per_s": X.n_rows / fit_s, "dtype": "f64",
+                      "path": "mfm_fwfm_fit_csr (host float64 buffers, transfers included)",
+                      "config": "FTRL alpha 0.05, beta 1, l1 1.0 / 0.1, batch 1024, 1 epoch, "
+                                "200,000 rows"},
+            "cpu_baseline": {"value": cpu_fit, "unit": "train rows/s", "predict_rows_per_s":
+                             cpu_pred, "cores": 1, "kind": "port",
+                             "sample": f"one epoch of {n_c} rows (the reference's FwFM "
+                                       "training is serial, rust/src/fwfm.rs:1-9) and scoring "
+                                       "of the 200,000 rows on every host thread"}}
+    except Exception as exc:
+        res["fwfm"] = {"error": f"{type(exc).__name__}: {exc}"}
+
+    # ---- C4: softmax FM ----
+    try:
+        n4 = args.softmax_rows
+
+        def gpu_scores(Xg, w0g, wg, Vg):  # the planted per-class FMs, scored on the GPU
+            with DeviceModel("fm", Xg.n_features, Vg.shape[1], dtype="float64",
+                             device=local) as mg:
+                mg.set_params(w0g, wg, Vg)
+                return mg.predict_csr(Xg.indptr, Xg.indices, Xg.data)
+        X, yc, sw = WL.softmax_ctr(n4, 4, score_fn=gpu_scores)
+        C, k, d = 10, 8, X.n_features
+        V0 = rng.normal(0, 0.01, (C, d, k))
+        ro = WL.row_orders(n4, 3, 6)
+
+        def fitm(mod, cuda, Xf, yf, swf, rof):
+            w0, w, V = np.zeros(C), np.zeros((C, d)), V0.copy()
+            mod.fm_fit_multiclass_csr(Xf.indptr, Xf.indices, Xf.data, d, yf, swf, w0, w, V,
+                                      "adam", 1e-3, 1e-5, 1e-5, 0.1, 0.9, 0.999, 1e-8, rof,
+                                      2048, 0.0, 0.0, 1.0, use_cuda=cuda)
+            return w0, w, V
+        fitm(_rust, True, X, yc, sw, ro)
+        t = time.perf_counter()
+        w0, w, V = fitm(_rust, True, X, yc, sw, ro)
+        fit_s = time.perf_counter() - t
+        n_c = 20000
+        Xc = X.rows(0, n_c)
+        t = time.perf_counter()
+        fitm(O, False, Xc, yc[:n_c], sw[:n_c], np.arange(n_c)[None, :])
+        cpu_fit = n_c / (time.perf_counter() - t)
+        zm = X.nnz / X.n_rows  # mean nonzeros per row
+        bpr = 8 + zm * 12 + zm * C * (k + 1) * 4 + C * 8
+        res["softmax"] = {
+            "workload": f"C4: softmax FM C=10, k=8, ragged Poisson(30)+1 rows (mean "
+                        f"{zm:.1f} nonzeros), 1M features, {n4} rows",
+            "predict": scoring("fm", X, None, 0, k, w0, r32(w), r32(V), None, bpr, C=C),
+            "train": {"fit_s": fit_s, "rows_per_s": n4 * 3 / fit_s, "dtype": "f64",
+                      "path": "mfm_fm_fit_multiclass_csr (host float64 buffers, transfers "
+                              "included)",
+                      "config": "Adam 1e-3, batch 2048, 3 epochs, sample weights U(0.5, 2), "
+                                "label smoothing 0.1"},
+            "cpu_baseline": {"value": cpu_fit, "unit": "train rows/s", "cores": 1,
+                             "kind": "port",
+                             "sample": f"one epoch of {n_c} rows (the reference's multiclass "
+                                       "training is serial, rust/src/lib.rs:446-448)"}}
+    except Exception as exc:
+        res["softmax"] = {"error": f"{type(exc).__name__}: {exc}"}
+    return res
+
+
 def run_ours(args):
     import torch
 
@@ -795,6 +1035,8 @@ def run_ours(args):
     prep = None if args.no_prep else prep_measure(args, local, dev_t, L, _lib, X)
     libffm = (libffm_measure(local, dev_t)
               if rank == 0 and world == 1 and not args.no_libffm else None)
+    configs = (configs_measure(args, local, dev_t, L, _lib)
+               if rank == 0 and world == 1 and not args.no_configs else None)
     train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
     train_dp = (train_dp_measure(args, rank, world, local, dev_t, L, _lib)
                 if world > 1 and not args.no_train else None)
@@ -848,6 +1090,8 @@ def run_ours(args):
             line["libffm"] = libffm
         if train:
             line["train"] = train
+        if configs:
+            line.update(configs)
         if train_dp:
             line["train_dp"] = train_dp
         print(json.dumps(line), flush=True)
@@ -1012,6 +1256,10 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--no-libffm", action="store_true",
                     help="skip the libffm reader measurement")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the other configurations (ffm, fwfm, softmax keys)")
+    ap.add_argument("--softmax-rows", type=int, default=2_000_000,
+                    help="rows of the softmax configuration")
     ap.add_argument("--no-prep", action="store_true",
                     help="skip the device CSR canonicalisation measurement")
     ap.add_argument("--train-rows", type=int, default=TRAIN_ROWS)

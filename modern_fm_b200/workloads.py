@@ -184,8 +184,10 @@ def ctr_fm(n_rows, seed, n_numeric=13, n_cat=26, vocab=2**20, space=2**22, zipf_
 FWFM_VOCABS = (100_000, 80_000, 60_000, 50_000, 40_000, 25_000, 10_000, 5_000, 3_000)
 
 
-def fwfm_ctr(n_rows, seed, vocabs=FWFM_VOCABS, zipf_s=1.05, k=8, positive_rate=0.044):
-    """One-hot FwFM workload. Returns (Csr, y, field_ids)."""
+def fwfm_ctr(n_rows, seed, vocabs=FWFM_VOCABS, zipf_s=1.05, k=8, positive_rate=0.044,
+             labels=True):
+    """One-hot FwFM workload. Returns (Csr, y, field_ids); y is None when
+    `labels` is false (the planted-model scoring is skipped)."""
     rng = np.random.default_rng(seed)
     F = len(vocabs)
     offs = np.concatenate([[0], np.cumsum(vocabs)]).astype(np.int64)
@@ -195,6 +197,8 @@ def fwfm_ctr(n_rows, seed, vocabs=FWFM_VOCABS, zipf_s=1.05, k=8, positive_rate=0
     X = Csr(np.arange(0, n_rows * F + 1, F, dtype=np.int64), idx.ravel().astype(np.int64),
             np.ones(n_rows * F), d)
     field_ids = np.repeat(np.arange(F, dtype=np.int64), vocabs)
+    if not labels:
+        return X, None, field_ids
     prng = np.random.default_rng(seed + 1_000_003)
     r = prng.uniform(0.0, 1.0, size=(F, F))
     V = prng.normal(0.0, 0.2, size=(d, k))
@@ -208,8 +212,11 @@ def fwfm_ctr(n_rows, seed, vocabs=FWFM_VOCABS, zipf_s=1.05, k=8, positive_rate=0
     return X, y, field_ids
 
 
-def softmax_ctr(n_rows, seed, n_features=1_000_000, n_classes=10, mean_nnz=30, k=8):
-    """Ragged multiclass workload. Returns (Csr, y (int64), sample_weight)."""
+def softmax_ctr(n_rows, seed, n_features=1_000_000, n_classes=10, mean_nnz=30, k=8,
+                score_fn=None):
+    """Ragged multiclass workload. Returns (Csr, y (int64), sample_weight).
+    `score_fn(X, w0, w, V)` scores the planted per-class FMs (default: scipy
+    on the host; a GPU scorer gives the same labels up to rounding, faster)."""
     rng = np.random.default_rng(seed)
     z = rng.poisson(mean_nnz, size=n_rows) + 1
     indptr = np.concatenate([[0], np.cumsum(z)]).astype(np.int64)
@@ -224,7 +231,7 @@ def softmax_ctr(n_rows, seed, n_features=1_000_000, n_classes=10, mean_nnz=30, k
     for c in range(n_classes):
         w = prng.normal(0.0, 0.1, size=n_features)
         V = prng.normal(0.0, 0.1, size=(n_features, k))
-        logits[:, c] = _fm_scores(X, 0.0, w, V)
+        logits[:, c] = (score_fn or _fm_scores)(X, 0.0, w, V)
     logits += rng.gumbel(size=logits.shape)
     y = logits.argmax(axis=1).astype(np.int64)
     sw = rng.uniform(0.5, 2.0, size=n_rows)
