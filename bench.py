@@ -465,6 +465,7 @@ def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
         t1.record(stream)
         torch.cuda.synchronize()
         ms = max_over_ranks(t0.elapsed_time(t1) / args.train_steps, world)
+        batches_ms = max_over_ranks(_lib.fit_phase_seconds()["batches"] * 1e3, world)
     finally:
         group.close()
     parity = None
@@ -488,7 +489,87 @@ def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
                       "split over the ranks, NCCL allreduce per batch)",
             "value": n / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "rows": n,
             "dtype": "f64", "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong",
-            "parity": parity}
+            "batches_ms_per_epoch": batches_ms, "parity": parity}
+
+
+def softmax_dp_measure(args, rank, world, local, dev_t, L, _lib):
+    """C4 (softmax FM C=10, k=8, Adam 1e-3, batch 2048, 3 epochs, sample
+    weights, label smoothing 0.1, ragged rows over 1M features) as ONE
+    data-parallel fit across all ranks (N > 1; mfm_fit_csr_dp, host float64
+    buffers): each global batch of 2048 rows split over the ranks, the batch's
+    touched-key gradient sums (C x (k + 1) per key) summed with NCCL, the
+    identical step on every rank. Strong scaling of one fit: rows/s = 3 epochs
+    x rows / time, max over ranks; the device time of the epochs' batches
+    (plans and transfers excluded) beside the wall time. Parity: rank 0 fits
+    the same problem on its GPU alone (float64, 1e-7 relative / 1e-9
+    absolute)."""
+    from modern_fm_b200 import _rust
+    from modern_fm_b200 import dp as DP
+    from modern_fm_b200 import workloads as WL
+    from modern_fm_b200.model import DeviceModel
+
+    n4 = args.softmax_rows
+
+    def gpu_scores(Xg, w0g, wg, Vg):
+        with DeviceModel("fm", Xg.n_features, Vg.shape[1], dtype="float64", device=local) as mg:
+            mg.set_params(w0g, wg, Vg)
+            return mg.predict_csr(Xg.indptr, Xg.indices, Xg.data)
+    X, yc, sw = WL.softmax_ctr(n4, 4, score_fn=gpu_scores)
+    C, k, d = 10, 8, X.n_features
+    V0 = np.random.default_rng(0).normal(0, 0.01, (C, d, k))
+    ro = WL.row_orders(n4, 3, 6)
+
+    def fresh():
+        w0, w, V = np.zeros(C), np.zeros((C, d)), V0.copy()
+        st = [[np.zeros_like(p) for _ in range(3)] for p in (w0, w, V)]
+        groups = [_lib.Group(_lib.ptr(p), None, *[_lib.ptr(a) for a in s3], None, None)
+                  for p, s3 in zip((w0, w, V), st)]
+        return (w0, w, V), st, groups
+
+    def train(rows_order):
+        return _lib.Train(0, _lib.OPTIMIZERS["adam"], 1e-3, 0.0, 1e-5, 0.0, 1e-5, 0.9, 0.999,
+                          1e-8, 1.0, 0.1, _lib.ptr(rows_order, _lib.i64p), rows_order.shape[0],
+                          2048)
+    group = DP.DataParallelGroup(device=local)
+    try:
+        ro1 = np.ascontiguousarray(ro[:1])
+        p, st, g = fresh()
+        group.fit_csr("fm", (X.indptr, X.indices, X.data), d, yc, sw, g, train(ro1), k,
+                      n_classes=C)  # warm-up: one epoch
+        p, st, g = fresh()
+        barrier(world)
+        t = time.perf_counter()
+        group.fit_csr("fm", (X.indptr, X.indices, X.data), d, yc, sw, g, train(ro), k,
+                      n_classes=C)
+        wall = max_over_ranks(time.perf_counter() - t, world)
+        ph = _lib.fit_phase_seconds()
+        batches = max_over_ranks(ph["batches"], world)
+    finally:
+        group.close()
+    parity = None
+    if rank == 0:
+        w0s, ws, Vs = np.zeros(C), np.zeros((C, d)), V0.copy()
+        t = time.perf_counter()
+        _rust.fm_fit_multiclass_csr(X.indptr, X.indices, X.data, d, yc, sw, w0s, ws, Vs, "adam",
+                                    1e-3, 1e-5, 1e-5, 0.1, 0.9, 0.999, 1e-8, ro, 2048, 0.0, 0.0,
+                                    1.0, use_cuda=True)
+        one_wall = time.perf_counter() - t
+        one_batches = _lib.fit_phase_seconds()["batches"]
+        ok = all(np.allclose(a, b, rtol=1e-7, atol=1e-9) for a, b in zip(p, (w0s, ws, Vs)))
+        parity = {"ok": bool(ok), "max_abs_dV": float(np.abs(p[2] - Vs).max()),
+                  "one_gpu_fit_s": one_wall, "one_gpu_batches_s": one_batches,
+                  "tolerance": "rank 0's parameters against a one-GPU fit of the same epochs: "
+                               "rtol 1e-7, atol 1e-9 (float64, sums in another order)"}
+    barrier(world)
+    if rank != 0:
+        return None
+    return {"metric": "softmax FM (C=10, k=8, Adam) data-parallel training rows/s (one fit, "
+                      "global batch 2048 split over the ranks, NCCL allreduce of the batch's "
+                      "touched-key sums)",
+            "value": 3 * n4 / wall, "unit": "rows/s", "n_gpus": world, "rows": n4,
+            "epochs": 3, "dtype": "f64", "fit_s": wall, "batches_s": batches,
+            "batches_rows_per_s": 3 * n4 / batches, "scaling": "strong", "parity": parity,
+            "path": "mfm_fit_csr_dp (host float64 buffers, transfers included in fit_s)"}
 
 
 PREP_BYTES_PER_ENTRY = 8 + 8 + 4 + 8  # int64 + float64 read, int32 + float64 written
@@ -891,6 +972,16 @@ def run_ours(args):
     dev_t = torch.device("cuda", local)
     torch.cuda.set_device(dev_t)
     L = _lib.lib()
+    if args.dp_only:  # data-parallel measurements only (N > 1)
+        out = {"n_gpus": world,
+               "train_dp": train_dp_measure(args, rank, world, local, dev_t, L, _lib),
+               "softmax_dp": softmax_dp_measure(args, rank, world, local, dev_t, L, _lib)}
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+        return
     if args.train_only:
         train = train_measure(args, rank, world, local, dev_t, L, _lib)
         train_dp = train_dp_measure(args, rank, world, local, dev_t, L, _lib) if world > 1 else None
@@ -1040,6 +1131,8 @@ def run_ours(args):
     train = None if args.no_train else train_measure(args, rank, world, local, dev_t, L, _lib)
     train_dp = (train_dp_measure(args, rank, world, local, dev_t, L, _lib)
                 if world > 1 and not args.no_train else None)
+    softmax_dp = (softmax_dp_measure(args, rank, world, local, dev_t, L, _lib)
+                  if world > 1 and not args.no_train and not args.no_configs else None)
 
     if rank == 0:
         rows_total = N_ROWS * world
@@ -1094,6 +1187,8 @@ def run_ours(args):
             line.update(configs)
         if train_dp:
             line["train_dp"] = train_dp
+        if softmax_dp:
+            line["softmax_dp"] = softmax_dp
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -1256,6 +1351,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     ap.add_argument("--no-libffm", action="store_true",
                     help="skip the libffm reader measurement")
+    ap.add_argument("--dp-only", action="store_true",
+                    help="only the data-parallel training measurements (N > 1)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the other configurations (ffm, fwfm, softmax keys)")
     ap.add_argument("--softmax-rows", type=int, default=2_000_000,

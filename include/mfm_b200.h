@@ -378,15 +378,38 @@ int mfm_dp_create(const unsigned char id[128], int world, int rank, int device, 
 int mfm_dp_destroy(mfm_dp* dp);
 
 /* mfm_fm_fit_device across the group (same arguments; the device is the
- * group's). Binary FM with k = 4, 8, 16, 32 (float32) or 2, 4, 8, 16
- * (float64); other shapes return MFM_ERR_UNSUPPORTED. Every rank must call it
- * with the same data, row orders and hyperparameters; results are identical
- * on every rank. */
+ * group's). Every rank must call it with the same data, row orders and
+ * hyperparameters; results are identical on every rank. */
 int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr, const int32_t* indices,
                          const void* data, int64_t n_rows, int64_t n_features, const void* y,
                          const void* sample_weight, const int32_t* row_orders,
                          const mfm_train* tr, int64_t k, mfm_dev_group* w0, mfm_dev_group* w,
                          mfm_dev_group* v, void* stream);
+
+/* Any fit of the host-buffer entry points above — FM, FFM or FwFM
+ * (model = MFM_MODEL_*), binary (n_classes = 1: y, float64 labels) or
+ * multiclass softmax (n_classes = C >= 2: ycls, class ids) — run as one
+ * data-parallel fit across the group: the same arguments, layouts, in-place
+ * updates and results as mfm_fm_fit_csr / mfm_fm_fit_multiclass_csr /
+ * mfm_ffm_fit_csr / mfm_ffm_fit_multiclass_csr / mfm_fwfm_fit_csr /
+ * mfm_fwfm_fit_multiclass_csr on the group's device (field_ids / n_fields for
+ * FFM and FwFM, r for FwFM; NULL otherwise). Every rank calls it with the
+ * same data, row orders, initial parameters and hyperparameters; each global
+ * batch's rows are split into `world` contiguous slices, each rank's gradient
+ * sums over the batch's touched keys are summed across ranks (NCCL), and every
+ * rank applies the identical step, so every rank ends with the same
+ * parameters, equal to a one-GPU fit up to summation order. No reference
+ * counterpart (the reference trains on one device). */
+int mfm_fit_csr_dp(mfm_dp* dp, int dtype, int model, int64_t n_classes, const mfm_csr* x,
+                   const double* y, const int64_t* ycls, const double* sample_weight,
+                   const int64_t* field_ids, int64_t n_fields, const mfm_train* tr, int64_t k,
+                   mfm_group* w0, mfm_group* w, mfm_group* v, mfm_group* r);
+
+/* Device time (seconds, CUDA events) of the calling thread's last fit, by
+ * phase: out[0] uploads and setup, out[1] the epochs' plans (sorts), out[2]
+ * the epochs' batches, out[3] the download of parameters and state. No
+ * reference counterpart (diagnostics). */
+void mfm_fit_phase_seconds(double out[4]);
 
 /* Release the engine's cached device memory on every device. */
 void mfm_release_cached_memory(void);

@@ -95,6 +95,10 @@ _SIGNATURES = {
                                         ct.c_void_p, ct.c_int64, ct.c_int64, ct.c_void_p,
                                         ct.c_void_p, ct.c_void_p, ct.POINTER(Train), ct.c_int64]
                              + [ct.POINTER(DevGroup)] * 3 + [ct.c_void_p]),
+    "mfm_fit_csr_dp": (ct.c_int, [ct.c_void_p, ct.c_int, ct.c_int, ct.c_int64, ct.POINTER(Csr),
+                                  f64p, i64p, f64p, i64p, ct.c_int64, ct.POINTER(Train),
+                                  ct.c_int64] + [ct.POINTER(Group)] * 4),
+    "mfm_fit_phase_seconds": (None, [ct.POINTER(ct.c_double)]),
     "mfm_csr_prep_device": (ct.c_int, [ct.c_int, ct.c_int, ct.c_int64, ct.c_int64, ct.c_int64,
                                        ct.c_void_p, ct.c_void_p, ct.c_void_p, ct.c_void_p,
                                        ct.c_void_p, ct.c_void_p, i64p, ct.c_void_p]),
@@ -207,3 +211,11 @@ def exec_options(dtype=None, device=None, n_devices=None):
     dev = int(device if device is not None else os.environ.get("MFM_B200_DEVICE", "0"))
     nd = int(n_devices if n_devices is not None else os.environ.get("MFM_B200_NUM_GPUS", "1"))
     return Exec(code, dev, max(1, nd))
+
+
+def fit_phase_seconds() -> dict:
+    """Device seconds of the calling thread's last fit by phase (upload,
+    plan, batches, download)."""
+    out = (ct.c_double * 4)()
+    lib().mfm_fit_phase_seconds(out)
+    return dict(zip(("upload", "plan", "batches", "download"), list(out)))

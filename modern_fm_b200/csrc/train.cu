@@ -57,35 +57,43 @@ namespace mfm {
 
 // Phase timing on the training stream, printed to stderr when the
 // environment variable MFM_B200_TIMING is set (diagnostics only).
+// Phase times of the calling thread's last fit (seconds): upload, plan,
+// batches, download (mfm_fit_phase_seconds).
+thread_local double g_phase_s[4] = {0.0, 0.0, 0.0, 0.0};
+
 struct PhaseTimer {
-    bool on = false;
+    bool print = false;
     cudaStream_t s = nullptr;
     cudaEvent_t last = nullptr;
     std::string report;
     explicit PhaseTimer(cudaStream_t st) : s(st) {
         const char* e = getenv("MFM_B200_TIMING");
-        on = e && *e && *e != '0';
-        if (on) {
-            cudaEventCreate(&last);
-            cudaEventRecord(last, s);
-        }
+        print = e && *e && *e != '0';
+        for (double& v : g_phase_s) v = 0.0;
+        if (cudaEventCreate(&last) == cudaSuccess) cudaEventRecord(last, s);
     }
+    // marks the end of a phase on stream s (the engine synchronises at every
+    // phase boundary anyway: uploads, the plan's host round trips, the end of
+    // an epoch's batches)
     void mark(const char* name) {
-        if (!on) return;
+        if (!last) return;
         cudaEvent_t now;
-        cudaEventCreate(&now);
+        if (cudaEventCreate(&now) != cudaSuccess) return;
         cudaEventRecord(now, s);
         cudaEventSynchronize(now);
         float ms = 0.f;
         cudaEventElapsedTime(&ms, last, now);
         cudaEventDestroy(last);
         last = now;
-        report += fmt(" %s=%.3fms", name, ms);
+        const std::string n(name);
+        const int slot = n == "upload" || n == "setup" ? 0 : n == "plan" ? 1
+                         : n == "batches" ? 2 : n == "download" ? 3 : -1;
+        if (slot >= 0) g_phase_s[slot] += ms * 1e-3;
+        if (print) report += fmt(" %s=%.3fms", name, ms);
     }
     ~PhaseTimer() {
-        if (!on) return;
         if (last) cudaEventDestroy(last);
-        fprintf(stderr, "mfm timing:%s\n", report.c_str());
+        if (print) fprintf(stderr, "mfm timing:%s\n", report.c_str());
     }
 };
 
@@ -136,6 +144,8 @@ struct NcclApi {
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    ncclResult_t (*GroupStart)() = nullptr;
+    ncclResult_t (*GroupEnd)() = nullptr;
 };
 inline const NcclApi& nccl() {
     static const NcclApi api = [] {
@@ -150,10 +160,13 @@ inline const NcclApi& nccl() {
         a.CommAbort = (decltype(a.CommAbort))dlsym(h, "ncclCommAbort");
         a.CommGetAsyncError = (decltype(a.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
         a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
+        a.GroupStart = (decltype(a.GroupStart))dlsym(h, "ncclGroupStart");
+        a.GroupEnd = (decltype(a.GroupEnd))dlsym(h, "ncclGroupEnd");
         return a;
     }();
     if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.CommDestroy ||
-        !api.CommAbort || !api.CommGetAsyncError || !api.GetErrorString)
+        !api.CommAbort || !api.CommGetAsyncError || !api.GetErrorString || !api.GroupStart ||
+        !api.GroupEnd)
         fail(MFM_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
     return api;
 }
@@ -220,7 +233,8 @@ struct Stream {
     DevBuf<uint32_t> rkey;    // key of each run
     DevBuf<int64_t> brun;     // runs before each batch (nb + 1)
     std::vector<int64_t> h_run;
-    DevBuf<T> grad;           // (max runs per batch + 1, TW)
+    DevBuf<T> grad;           // (max runs per batch + 1, TW or Wp)
+    std::vector<int64_t> h_estart;  // payload path, data-parallel: entry start per position
 };
 
 template <class T>
@@ -498,7 +512,21 @@ struct Trainer {
         st_.h_long.resize(nb + 1);
         d2h(st_.h_item.data(), st_.bitem.ptr, nb + 1, s, "plan download");
         d2h(st_.h_long.data(), st_.blong.ptr, nb + 1, s, "plan download");
+        if (dp) {  // data-parallel: the runs of each batch index its cross-rank sums
+            st_.brun.alloc(device, nb + 1);
+            batch_runs_kernel<<<blocks_for(nb + 1, 256), 256, 0, s>>>(st_.seg_lo.ptr, nb,
+                                                                    run_id.ptr, st_.brun.ptr);
+            MFM_CHECK_LAUNCH("plan");
+            st_.h_run.resize(nb + 1);
+            d2h(st_.h_run.data(), st_.brun.ptr, nb + 1, s, "plan download");
+        }
         MFM_CUDA(cudaStreamSynchronize(s), "plan");
+        if (dp) {
+            int64_t mr = 0;
+            for (int64_t b = 0; b < nb; ++b) mr = std::max(mr, st_.h_run[b + 1] - st_.h_run[b]);
+            if (st_.grad.n < (size_t)((mr + 1) * st_.Wp) || !st_.grad.ptr)
+                st_.grad.alloc(device, (mr + 1) * st_.Wp);
+        }
         st_.max_items = 0;
         for (int64_t b = 0; b < nb; ++b)
             st_.max_items = std::max(st_.max_items, st_.h_item[b + 1] - st_.h_item[b]);
@@ -534,6 +562,14 @@ struct Trainer {
         R.gw0 = G[0];
         R.do_w0 = 0;
         R.nrows = 0;
+        R.dp = 0;
+        R.vals = nullptr;
+        R.olo = R.ohi = 0;
+        R.item_run = st_.item_run.ptr;
+        R.run0 = R.nrun = 0;
+        R.grad = nullptr;
+        R.progress = nullptr;
+        R.pstep = 0;
         return R;
     }
 
@@ -823,11 +859,29 @@ struct Trainer {
         }
     }
 
-    void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz, int64_t nrows, bool do_w0) {
+    // Stage 1 and stage 2 of batch b on stream st_. Data-parallel: this
+    // rank's rows are [rlo, rhi) of the batch (grow holds them from 0); the
+    // sums land in st_.grad and reduce_apply_kernel steps them after the
+    // cross-rank sum (launch_dp_apply).
+    void launch_reduce(Stream<T>& st_, int64_t b, T inv_bsz, int64_t nrows, bool do_w0,
+                       int64_t rlo = 0, int64_t rhi = 0) {
         constexpr int VEC = 16 / (int)sizeof(T);
         const int64_t i0 = st_.h_item[b], i1 = st_.h_item[b + 1];
         const int64_t l0 = st_.h_long[b], l1 = st_.h_long[b + 1];
         RedArgs<T> R = red_args(st_, b, inv_bsz);
+        if (dp) {
+            const int64_t pos0 = b * B;
+            int64_t e[2] = {0, 0};
+            d_entry_bounds(st_, pos0 + rlo, pos0 + rhi, e);
+            R.dp = 1;
+            R.vals = st_.vals + st_.h_seg[b];
+            R.olo = (uint32_t)(e[0] - st_.h_seg[b]);
+            R.ohi = (uint32_t)(e[1] - st_.h_seg[b]);
+            R.run0 = st_.h_run[b];
+            R.nrun = st_.h_run[b + 1] - st_.h_run[b];
+            R.grad = st_.grad.ptr;
+            nrows = rhi - rlo;  // the w0 sum covers this rank's rows
+        }
         if (i1 > i0) {
             const int64_t warps = ceil_div(i1 - i0, R.gpw);
             reduce_items_kernel<T, VEC><<<blocks_for(warps, 8), 256, 0, s>>>(R, i1 - i0);
@@ -1052,15 +1106,74 @@ struct Trainer {
         MFM_CUDA(cudaStreamSynchronize(s), "training");
     }
 
+    // Epoch-order entry ids [e0, e1) of epoch positions [p0, p1) on stream
+    // st_ (the plan's entry starts, host copy made per epoch).
+    void d_entry_bounds(const Stream<T>& st_, int64_t p0, int64_t p1, int64_t* e) {
+        e[0] = st_.h_estart[p0];
+        e[1] = st_.h_estart[p1];
+    }
+
+    // Data-parallel: the cross-rank sum of every stream's batch sums (one NCCL
+    // group), then the identical step on every rank.
+    void launch_dp_apply(int64_t b, T inv_bsz, uint32_t step) {
+        constexpr int VEC = 16 / (int)sizeof(T);
+        MFM_CHECK_LAUNCH("reduce");
+        ncclResult_t r = nccl().GroupStart();
+        for (int si = 0; si < n_streams && r == ncclSuccess; ++si) {
+            Stream<T>& st_ = S[si];
+            const size_t cnt = (size_t)(st_.h_run[b + 1] - st_.h_run[b] + 1) * st_.Wp;
+            r = nccl().AllReduce(st_.grad.ptr, st_.grad.ptr, cnt,
+                                 sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum, dp->comm,
+                                 s);
+        }
+        const ncclResult_t r2 = nccl().GroupEnd();
+        if (r == ncclSuccess) r = r2;
+        if (r != ncclSuccess) {  // e.g. a peer process exited: abort, then drain
+            nccl().CommAbort(dp->comm);
+            dp->aborted = true;
+            cudaStreamSynchronize(s);
+            fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group was "
+                                   "aborted", nccl().GetErrorString(r)));
+        }
+        for (int si = 0; si < n_streams; ++si) {
+            Stream<T>& st_ = S[si];
+            RedArgs<T> R = red_args(st_, b, inv_bsz);
+            R.dp = 1;
+            R.run0 = st_.h_run[b];
+            R.nrun = st_.h_run[b + 1] - st_.h_run[b];
+            R.grad = st_.grad.ptr;
+            R.do_w0 = si == n_streams - 1 ? 1 : 0;
+            R.progress = R.do_w0 ? dp->prog_d : nullptr;
+            R.pstep = step;
+            const int64_t warps = std::max<int64_t>(1, ceil_div(R.nrun, R.gpw));
+            reduce_apply_kernel<T, VEC><<<blocks_for(warps, 8), 256, 0, s>>>(R);
+        }
+        MFM_CHECK_LAUNCH("data-parallel apply");
+    }
+
     void run(const FwdArgs<T>& base, PhaseTimer& pt) {
         if (S[0].tab) {
             run_tab(base, pt);
             return;
         }
+        uint32_t gstep = 0;  // batches enqueued in this call (data-parallel liveness)
+        if (dp) {
+            if (dp->aborted)
+                fail(MFM_ERR_INVALID, "the data-parallel group was aborted; create a new one");
+            *(volatile unsigned*)dp->prog_h = 0u;
+        }
         for (int64_t e = 0; e < E; ++e) {
-            for (int si = 0; si < n_streams; ++si) plan(S[si], (int)e);
+            for (int si = 0; si < n_streams; ++si) {
+                plan(S[si], (int)e);
+                if (dp) {  // entry starts by position, for each rank's entry-id range
+                    S[si].h_estart.resize(n_rows + 1);
+                    d2h(S[si].h_estart.data(), S[si].estart.ptr, n_rows + 1, s,
+                        "plan download");
+                    MFM_CUDA(cudaStreamSynchronize(s), "plan");
+                }
+            }
             pt.mark("plan");
-            {
+            if (!dp) {
                 FwdArgs<T> A = base;
                 A.order = p_order + e * n_rows;
                 A.estart1 = S[0].estart.ptr;
@@ -1075,10 +1188,16 @@ struct Trainer {
             for (int64_t b = 0; b < nb; ++b) {
                 const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                 const T inv_bsz = T(1) / (T)nrows;  // divide by batch length (fm.rs:395-398)
+                // data-parallel: this rank scores rows [rlo, rhi) of the batch, and
+                // stays at most kDpAhead batches ahead of the device
+                const int64_t rlo = dp ? nrows * dp->rank / dp->world : 0;
+                const int64_t rhi = dp ? nrows * (dp->rank + 1) / dp->world : nrows;
+                ++gstep;
+                if (dp && gstep > kDpAhead) dp_wait(gstep - kDpAhead);
                 FwdArgs<T> A = base;
                 A.order = p_order + e * n_rows;
-                A.pos0 = pos0;
-                A.nrows = nrows;
+                A.pos0 = pos0 + rlo;
+                A.nrows = rhi - rlo;
                 A.estart1 = S[0].estart.ptr;
                 A.seg1 = S[0].h_seg[b];
                 A.pay1 = S[0].pay.ptr;
@@ -1091,10 +1210,12 @@ struct Trainer {
                     A.W2 = S[1].Wp;
                     A.inv2 = S[1].inv.ptr;
                 }
-                launch_forward(A, nrows);
+                launch_forward(A, rhi - rlo);
                 for (int si = 0; si < n_streams; ++si)
-                    launch_reduce(S[si], b, inv_bsz, nrows, si == n_streams - 1);
+                    launch_reduce(S[si], b, inv_bsz, nrows, si == n_streams - 1, rlo, rhi);
+                if (dp) launch_dp_apply(b, inv_bsz, gstep);
             }
+            if (dp) dp_wait(gstep);  // the epoch's last batch, before the next plan
             pt.mark("batches");
         }
         MFM_CUDA(cudaStreamSynchronize(s), "training");
@@ -1157,11 +1278,12 @@ void validate_fit(const FitSpec& f) {
 }
 
 template <class T>
-void fit_impl(const FitSpec& f, int device) {
+void fit_impl(const FitSpec& f, int device, mfm_dp* dp = nullptr) {
     DeviceGuard guard(device);
     std::lock_guard<std::mutex> lk(device_mutex(device));
     Trainer<T> tr;
     tr.device = device;
+    tr.dp = dp;
     tr.s = device_stream(device);
     cudaStream_t s = tr.s;
     PhaseTimer pt(s);
@@ -1254,16 +1376,16 @@ void fit_impl(const FitSpec& f, int device) {
     pt.mark("download");
 }
 
-void fit_dispatch(const FitSpec& f, const mfm_exec* ex) {
+void fit_dispatch(const FitSpec& f, const mfm_exec* ex, mfm_dp* dp = nullptr) {
     validate_fit(f);
     const int dtype = ex ? ex->dtype : MFM_DTYPE_F64;
-    const int device = ex ? ex->device : 0;
+    const int device = dp ? dp->device : ex ? ex->device : 0;
     // float32 parameters with float64 arithmetic train as the reference does:
     // float64 parameters and state for the whole fit (_backend.py:116-130)
     if (dtype == MFM_DTYPE_F64 || dtype == MFM_DTYPE_F32_F64)
-        fit_impl<double>(f, device);
+        fit_impl<double>(f, device, dp);
     else if (dtype == MFM_DTYPE_F32)
-        fit_impl<float>(f, device);
+        fit_impl<float>(f, device, dp);
     else
         fail(MFM_ERR_INVALID, fmt("unknown dtype %d", dtype));
 }
@@ -1374,11 +1496,6 @@ void fm_fit_device_impl(int device, cudaStream_t s, const int64_t* indptr,
     tr.device_group(1, w, n_features, 1, 0);
     tr.device_group(2, v, n_features * k, k, 1);
     FwdArgs<T> A = tr.prepare(c, data, y, nullptr, sw);
-    if (dp && !tr.S[0].tab)
-        fail(MFM_ERR_UNSUPPORTED,
-             fmt("data-parallel training supports k = %d, %d, %d or %d in this dtype, got %lld",
-                 16 / (int)sizeof(T), 32 / (int)sizeof(T), 64 / (int)sizeof(T),
-                 128 / (int)sizeof(T), (long long)k));
     pt.mark("setup");
     if (n_rows > 0) tr.run(A, pt);
 }
@@ -1498,4 +1615,30 @@ extern "C" int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr
         fit_device_dispatch(dtype, dp->device, indptr, indices, data, n_rows, n_features, y,
                             sample_weight, row_orders, tr, k, w0, w, v, stream, dp);
     });
+}
+
+extern "C" int mfm_fit_csr_dp(mfm_dp* dp, int dtype, int model, int64_t n_classes,
+                              const mfm_csr* x, const double* y, const int64_t* ycls,
+                              const double* sample_weight, const int64_t* field_ids,
+                              int64_t n_fields, const mfm_train* tr, int64_t k, mfm_group* w0,
+                              mfm_group* w, mfm_group* v, mfm_group* r) {
+    return guarded([&] {
+        if (!dp) fail(MFM_ERR_INVALID, "a data-parallel group must be provided");
+        if (n_classes < 1) fail(MFM_ERR_INVALID, "n_classes must be >= 1");
+        const Model m = model == MFM_MODEL_FM    ? M_FM
+                        : model == MFM_MODEL_FFM ? M_FFM
+                        : model == MFM_MODEL_FWFM
+                            ? M_FWFM
+                            : (fail(MFM_ERR_INVALID, fmt("unknown model kind %d", model)), M_FM);
+        const bool mc = n_classes > 1;
+        FitSpec f{m, mc, n_classes, x, mc ? nullptr : y, mc ? ycls : nullptr, sample_weight,
+                  m == M_FM ? nullptr : field_ids, m == M_FM ? 0 : n_fields, tr, k, w0, w, v,
+                  m == M_FWFM ? r : nullptr};
+        const mfm_exec ex{dtype, dp->device, 1};
+        fit_dispatch(f, &ex, dp);
+    });
+}
+
+extern "C" void mfm_fit_phase_seconds(double out[4]) {
+    for (int i = 0; i < 4; ++i) out[i] = mfm::g_phase_s[i];
 }

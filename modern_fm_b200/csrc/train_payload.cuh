@@ -28,7 +28,28 @@ struct RedArgs {
     int64_t nrows;
     int C, do_w0;
     GroupDev<T> gw0;
+    // data-parallel batch (dp != 0): only this rank's entries, those whose
+    // batch-local entry id vals[p] lies in [olo, ohi), are summed; the run sums
+    // go to grad (batch-local run index, stride Wp; row nrun: the w0 sum per
+    // class over this rank's rows, grow[0, nrows)) instead of the optimizer,
+    // which reduce_apply_kernel runs after the cross-rank sum
+    int dp;
+    const uint32_t* vals;       // batch-local entry id per batch-local sorted position
+    uint32_t olo, ohi;
+    const int64_t* item_run;    // epoch run of each item
+    int64_t run0, nrun;         // this batch's runs: [run0, run0 + nrun)
+    T* grad;
+    unsigned* progress;         // mapped host word, set to pstep by the apply
+    unsigned pstep;
 };
+
+template <class T, int VEC>
+__device__ __forceinline__ void store_vec(T* dst, const T* v) {
+    Vec<T, VEC> o;
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) o.v[c] = v[c];
+    *reinterpret_cast<Vec<T, VEC>*>(dst) = o;
+}
 
 // Steps the scalar columns [vv*VEC, vv*VEC + VEC) of key `key` (those below
 // W) with column sums `sum`: every column's loads are issued before the first
@@ -81,20 +102,35 @@ __device__ __forceinline__ void reduce_items_dev(const RedArgs<T>& R, int64_t n_
     const bool multi = (d.cnt & kMultiItem) != 0;
     const T* rows = R.pay + (d.p0 - R.seg) * R.Wp;
     for (int vv = vl; vv < R.nv; vv += R.nvs) {
-        const bool vec = !multi && vec_in_group0<T, VEC>(R, vv);
+        const bool vec = !R.dp && !multi && vec_in_group0<T, VEC>(R, vv);
         const int64_t idx0 = (int64_t)d.key * R.g0.width + vv * VEC;
         VecStep<T, VEC> st;
         if (vec) st.prefetch(R.g0, idx0, R.opt.kind);  // overlaps the payload loads
         T acc[VEC];
 #pragma unroll
         for (int c = 0; c < VEC; ++c) acc[c] = T(0);
+        if (!R.dp) {
 #pragma unroll 4
-        for (int q = 0; q < cnt; ++q) {
-            const Vec<T, VEC> x = ldg_vec<T, VEC>(rows + (int64_t)q * R.Wp + vv * VEC);
+            for (int q = 0; q < cnt; ++q) {
+                const Vec<T, VEC> x = ldg_vec<T, VEC>(rows + (int64_t)q * R.Wp + vv * VEC);
 #pragma unroll
-            for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+                for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+            }
+        } else {  // this rank's entries only (other ranks' payload rows are stale)
+            const uint32_t* ids = R.vals + (d.p0 - R.seg);
+#pragma unroll 4
+            for (int q = 0; q < cnt; ++q) {
+                const uint32_t id = ids[q];
+                if (id < R.olo || id >= R.ohi) continue;
+                const Vec<T, VEC> x = ldg_vec<T, VEC>(rows + (int64_t)q * R.Wp + vv * VEC);
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) acc[c] += x.v[c];
+            }
         }
-        if (multi) {
+        if (R.dp && !multi) {  // the run's sum for this rank, stepped after the cross-rank sum
+            store_vec<T, VEC>(R.grad + (R.item_run[R.item0 + it] - R.run0) * R.Wp + vv * VEC,
+                              acc);
+        } else if (multi) {
             Vec<T, VEC> o;
 #pragma unroll
             for (int c = 0; c < VEC; ++c) o.v[c] = acc[c];
@@ -159,7 +195,14 @@ __device__ __forceinline__ void w0_step_dev(const T* grow, int64_t nrows, int C,
 
 template <class T>
 __device__ __forceinline__ void w0_dev(const RedArgs<T>& R, T* sm) {
-    w0_step_dev(R.grow, R.nrows, R.C, R.inv_bsz, R.gw0, R.opt, sm);
+    if (!R.dp) {
+        w0_step_dev(R.grow, R.nrows, R.C, R.inv_bsz, R.gw0, R.opt, sm);
+        return;
+    }
+    for (int c = 0; c < R.C; ++c) {  // this rank's sums, stepped after the cross-rank sum
+        const T tot = block_sum_rows(R.grow, R.nrows, R.C, c, sm);
+        if (threadIdx.x == 0) R.grad[R.nrun * R.Wp + c] = tot;
+    }
 }
 
 template <class T, int VEC>
@@ -203,7 +246,9 @@ __device__ __forceinline__ void reduce_runs_dev(const RedArgs<T>& R, int64_t l0,
                     tot[c] = T(0);
                     for (int w = 0; w < 8; ++w) tot[c] += wsum[w][vl * VEC + c];
                 }
-                if (vec_in_group0<T, VEC>(R, vv)) {
+                if (R.dp) {  // stepped after the cross-rank sum
+                    store_vec<T, VEC>(R.grad + (r - R.run0) * R.Wp + vv * VEC, tot);
+                } else if (vec_in_group0<T, VEC>(R, vv)) {
                     const int64_t idx0 = (int64_t)key * R.g0.width + vv * VEC;
                     VecStep<T, VEC> st;
                     st.prefetch(R.g0, idx0, R.opt.kind);
@@ -230,6 +275,45 @@ __global__ void __launch_bounds__(256) reduce_runs_kernel(RedArgs<T> R, int64_t 
         return;
     }
     reduce_runs_dev<T, VEC>(R, l0, n_long, blockIdx.x, gridDim.x - 1, wsum);
+}
+
+// Data-parallel step (after the cross-rank sum of grad): lane groups of nvs
+// lanes, one run per group, the run's column sums stepped as stage 1 steps a
+// single-item run; w0 by thread 0 of block 0 when do_w0, which also records
+// the step in the progress word.
+template <class T, int VEC>
+__global__ void __launch_bounds__(256, 4) reduce_apply_kernel(RedArgs<T> R) {
+    const int lane = threadIdx.x & 31, grp = lane / R.nvs, vl = lane % R.nvs;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        if (R.do_w0)
+            for (int c = 0; c < R.C; ++c)
+                opt_step(R.gw0, c, R.grad[R.nrun * R.Wp + c] * R.inv_bsz, R.opt);
+        if (R.progress) *(volatile unsigned*)R.progress = R.pstep;
+    }
+    if (grp >= R.gpw) return;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t wi = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;; wi += nwarps) {
+        const int64_t j = wi * R.gpw + grp;
+        if (j >= R.nrun) return;
+        const uint32_t key = R.desc[R.item_start[R.run0 + j]].key;
+        const T* g = R.grad + j * R.Wp;
+        for (int vv = vl; vv < R.nv; vv += R.nvs) {
+            T acc[VEC];
+            const Vec<T, VEC> x = ldg_vec<T, VEC>(g + vv * VEC);
+#pragma unroll
+            for (int c = 0; c < VEC; ++c) acc[c] = x.v[c];
+            if (vec_in_group0<T, VEC>(R, vv)) {
+                const int64_t idx0 = (int64_t)key * R.g0.width + vv * VEC;
+                VecStep<T, VEC> st;
+                st.prefetch(R.g0, idx0, R.opt.kind);
+#pragma unroll
+                for (int c = 0; c < VEC; ++c) acc[c] *= R.inv_bsz;
+                st.commit(R.g0, idx0, acc, R.opt);
+            } else {
+                apply_cols<T, VEC>(R, key, vv, acc);
+            }
+        }
+    }
 }
 
 // --------------------------------------------------- persistent epoch loop --

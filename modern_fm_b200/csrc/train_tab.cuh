@@ -64,10 +64,12 @@ struct TabArgs {
     unsigned pstep;
 };
 
-// float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers)
+// float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers);
+// float64 with k <= 16 under SGD / AdaGrad 2 blocks (128 registers)
 template <class T, int NV, int OPT>
 constexpr int tab_min_blocks() {
-    return (sizeof(T) == 4 && NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? 4 : 1;
+    return (NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? (sizeof(T) == 4 ? 4 : 2)
+                                               : (sizeof(T) == 8 && NV <= 8 && OPT <= MFM_OPT_ADAGRAD ? 2 : 1);
 }
 
 template <class T, int VEC, int NV, int OPT>

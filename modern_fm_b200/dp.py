@@ -1,4 +1,4 @@
-"""Synchronous data-parallel FM training over NCCL (one process per GPU).
+"""Synchronous data-parallel FM / FFM / FwFM training over NCCL (one process per GPU).
 
 Every rank holds the whole training set, the parameters and the optimizer
 state. Each global mini-batch (the same row_orders chunking as one GPU) is cut
@@ -12,8 +12,9 @@ rust/src/fm.rs:373-411 (batch loop) and rust/src/optimizer.rs:48-167 (steps).
     import torch.distributed as dist
     dist.init_process_group("gloo")            # any backend: it carries the group id and
     group = DataParallelGroup(device=local_rank)  # the peer check before each fit
-    group.fm_fit_device(...)                    # every rank, same arguments
-    group.close()
+    group.fm_fit_device(...)                    # binary FM on device arrays, or
+    group.fit_csr(...)                          # any model, host buffers (every rank, same
+    group.close()                               # arguments)
 
 A rank that has left is found by the bounded barrier before each fit; a rank
 lost during a fit stops the device's progress, and the engine aborts the NCCL
@@ -120,6 +121,40 @@ class DataParallelGroup:
         rc = _lib.lib().mfm_fm_fit_device_dp(self._h, dtype, indptr, indices, data, n_rows,
                                              n_features, y, sample_weight, row_orders, train, k,
                                              w0, w, v, stream)
+        if rc != 0:
+            raise RuntimeError(_lib.last_error())
+
+    def fit_csr(self, model: str, x, n_features: int, y, sample_weight, params, train, k: int,
+                n_classes: int = 1, field_ids=None, n_fields: int | None = None,
+                dtype: str = "float64", check_peers_s: float | None = 60.0):
+        """mfm_fit_csr_dp: one fit of the reference's host-buffer layout across
+        the group. `model` is "fm", "ffm" or "fwfm"; x = (indptr, indices,
+        data) (int64 / int64 / float64); y float64 labels (binary,
+        n_classes = 1) or int64 class ids (multiclass); `params` a list of
+        _lib.Group for w0, w, V (and R for fwfm) over float64 arrays updated
+        in place; `train` an _lib.Train with row_orders set. Every rank calls
+        it with the same arguments; raises RuntimeError with the engine's
+        message on failure."""
+        import numpy as np
+
+        if check_peers_s is not None:
+            check_peers(check_peers_s, self._group)
+        kind = {"fm": _lib.MFM_MODEL_FM, "ffm": _lib.MFM_MODEL_FFM, "fwfm": _lib.MFM_MODEL_FWFM}
+        if model not in kind:
+            raise ValueError(f"model must be one of {sorted(kind)}")
+        csr, keep = _lib.make_csr(x[0], x[1], x[2], n_features)
+        mc = n_classes > 1
+        yv = np.ascontiguousarray(y, dtype=np.int64 if mc else np.float64)
+        sw = np.ascontiguousarray(sample_weight, dtype=np.float64)
+        fid = None if field_ids is None else np.ascontiguousarray(field_ids, dtype=np.int64)
+        if n_fields is None:
+            n_fields = 0 if fid is None or not fid.size else int(fid.max()) + 1
+        groups = list(params) + [None] * (4 - len(params))
+        rc = _lib.lib().mfm_fit_csr_dp(
+            self._h, _lib.dtype_code(dtype), kind[model], int(n_classes), ct.byref(csr),
+            None if mc else _lib.ptr(yv), _lib.ptr(yv, _lib.i64p) if mc else None,
+            _lib.ptr(sw), _lib.ptr(fid, _lib.i64p), n_fields, ct.byref(train), int(k),
+            *[ct.byref(g) if g is not None else None for g in groups])
         if rc != 0:
             raise RuntimeError(_lib.last_error())
 
