@@ -123,6 +123,35 @@ __global__ void __launch_bounds__(kFlatNT)
     if (bad && lane == 0) atomicOr(flags, bad);
 }
 
+// Sorts the row's (column << 32 | position) pairs staged in s[0, len) by a
+// bitonic network over the next power of two P >= len (padded with the
+// largest key), one warp: equal columns keep their original order (the
+// position breaks ties). O(P log^2 P / 64) steps per lane instead of the
+// O(len^2 / 32) rank loops a short row would otherwise take.
+__device__ __forceinline__ int warp_sort_row(uint64_t* s, int len, int lane) {
+    int P = 1;
+    while (P < len) P <<= 1;
+    for (int e = len + lane; e < P; e += 32) s[e] = ~0ull;
+    __syncwarp();
+    for (int k = 2; k <= P; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < (P >> 1); i += 32) {
+                const int a = 2 * j * (i / j) + (i % j), b = a + j;
+                const uint64_t x = s[a], y = s[b];
+                if ((x > y) == ((a & k) == 0)) {
+                    s[a] = y;
+                    s[b] = x;
+                }
+            }
+            __syncwarp();
+        }
+    return P;
+}
+
+__device__ __forceinline__ uint32_t sorted_col(const uint64_t* s, int e) {
+    return (uint32_t)(s[e] >> 32);
+}
+
 // flags[0]: kBad* / kUnsorted bits; flags[1]: number of long unsorted rows.
 template <class T>
 __global__ void __launch_bounds__(kPrepWarps * 32)
@@ -131,7 +160,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
                           int64_t n_features, int32_t* __restrict__ ind_out,
                           T* __restrict__ dat_out, int64_t* __restrict__ cnt,
                           int64_t* __restrict__ long_row, int64_t max_long, unsigned* flags) {
-    __shared__ int32_t skey[kPrepWarps][kShortRow];
+    __shared__ uint64_t skey[kPrepWarps][kShortRow];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
     for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
@@ -160,7 +189,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
             if (in) {
                 ind_out[q] = (int32_t)c;
                 dat_out[q] = (T)data[q];
-                if (short_row) skey[wib][q - lo] = (int32_t)c;
+                if (short_row)
+                    skey[wib][q - lo] = ((uint64_t)(uint32_t)c << 32) | (uint64_t)(q - lo);
             }
         }
         bad = __any_sync(0xffffffffu, bad);
@@ -176,13 +206,10 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
         if (unsorted) {
             if (short_row) {
                 __syncwarp();
-                int firsts = 0;  // entries whose column has no earlier occurrence
-                for (int e = lane; e < (int)len; e += 32) {
-                    const int32_t key = skey[wib][e];
-                    bool first = true;
-                    for (int e2 = 0; e2 < e; ++e2) first &= skey[wib][e2] != key;
-                    firsts += first;
-                }
+                warp_sort_row(skey[wib], (int)len, lane);
+                int firsts = 0;  // distinct columns: heads of the sorted row's runs
+                for (int e = lane; e < (int)len; e += 32)
+                    firsts += e == 0 || sorted_col(skey[wib], e) != sorted_col(skey[wib], e - 1);
                 count = warp_sum(firsts);
             } else {
                 count = 0;  // counted after the sort
@@ -210,9 +237,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
                           const double* __restrict__ data, int64_t n_rows,
                           const int64_t* __restrict__ out_ptr, int32_t* __restrict__ ind_out,
                           T* __restrict__ dat_out) {
-    __shared__ int32_t skey[kPrepWarps][kShortRow];
+    __shared__ uint64_t skey[kPrepWarps][kShortRow];
     __shared__ double sval[kPrepWarps][kShortRow];
-    __shared__ unsigned char sfirst[kPrepWarps][kShortRow];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
     for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
@@ -231,7 +257,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
             unsorted |= __any_sync(0xffffffffu, q < hi && q > lo && !(c > prev));
             carry = __shfl_sync(0xffffffffu, c, 31);
             if (short_row && q < hi) {
-                skey[wib][q - lo] = (int32_t)c;
+                skey[wib][q - lo] = ((uint64_t)(uint32_t)c << 32) | (uint64_t)(q - lo);
                 sval[wib][q - lo] = data[q];
             }
         }
@@ -244,23 +270,26 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
         }
         if (!short_row) continue;  // written by csr_prep_long_kernel from the sorted rows
         __syncwarp();
-        for (int e = lane; e < (int)len; e += 32) {
-            const int32_t key = skey[wib][e];
-            bool first = true;
-            for (int e2 = 0; e2 < e; ++e2) first &= skey[wib][e2] != key;
-            sfirst[wib][e] = first;
-        }
-        __syncwarp();
-        for (int e = lane; e < (int)len; e += 32) {
-            if (!sfirst[wib][e]) continue;
-            const int32_t key = skey[wib][e];
-            int rank = 0;  // distinct columns below this one
-            for (int e2 = 0; e2 < (int)len; ++e2) rank += sfirst[wib][e2] && skey[wib][e2] < key;
-            double sum = sval[wib][e];  // from the first occurrence, in original order
-            for (int e2 = e + 1; e2 < (int)len; ++e2)
-                if (skey[wib][e2] == key) sum += sval[wib][e2];
-            ind_out[o + rank] = key;
-            dat_out[o + rank] = (T)sum;
+        const uint64_t* sk = skey[wib];
+        warp_sort_row(skey[wib], (int)len, lane);
+        // heads of the sorted runs are the distinct columns in ascending order;
+        // a head's rank is the number of heads before it, and its sum adds the
+        // run's values in their original order, from the first occurrence
+        int before = 0;
+        for (int base = 0; base < (int)len; base += 32) {
+            const int e = base + lane;
+            const bool head = e < (int)len && (e == 0 || sorted_col(sk, e) != sorted_col(sk, e - 1));
+            const unsigned hm = __ballot_sync(0xffffffffu, head);
+            if (head) {
+                const int rank = before + __popc(hm & ((1u << lane) - 1u));
+                const uint32_t key = sorted_col(sk, e);
+                double sum = sval[wib][(uint32_t)sk[e]];
+                for (int e2 = e + 1; e2 < (int)len && sorted_col(sk, e2) == key; ++e2)
+                    sum += sval[wib][(uint32_t)sk[e2]];
+                ind_out[o + rank] = (int32_t)key;
+                dat_out[o + rank] = (T)sum;
+            }
+            before += __popc(hm);
         }
         __syncwarp();  // shared rows are rewritten by the next row
     }
