@@ -120,7 +120,9 @@ __global__ void __launch_bounds__(kFlatNT)
         }
     }
     bad = __reduce_or_sync(0xffffffffu, bad);
-    if (bad && lane == 0) atomicOr(flags, bad);
+    // flags only gain bits: once a bit is set, later warps skip the atomic on
+    // the one shared word (on unsorted input nearly every warp finds disorder)
+    if (bad && lane == 0 && (*(volatile unsigned*)flags & bad) != bad) atomicOr(flags, bad);
 }
 
 // Sorts the row's (column << 32 | position) pairs staged in s[0, len) by a
@@ -221,7 +223,8 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
                     if (slot < max_long) long_row[slot] = r;
                 }
             }
-            if (lane == 0) atomicOr(flags, kUnsorted);
+            if (lane == 0 && !(*(volatile unsigned*)flags & kUnsorted))
+                atomicOr(flags, kUnsorted);  // once set, later rows skip the atomic
         }
         __syncwarp();  // skey is rewritten by the next row
         if (lane == 0) cnt[r] = count;
