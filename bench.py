@@ -1238,106 +1238,6 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_suite(args):
-    """The other benchmark configurations through the reference-facing API
-    (host buffers in the boundary format, float32 compute): fit wall time and
-    training rows/s, and predict rows/s on the test rows. One JSON line each.
-    Data: the seeded synthetic stand-ins of `modern_fm_b200.workloads`."""
-    os.environ["MFM_B200_DTYPE"] = "float32"
-    from modern_fm_b200 import _rust
-    from modern_fm_b200 import workloads as WL
-
-    def timed(fn, reps=1):
-        fn()  # warm-up (first-call setup, allocator)
-        t = time.perf_counter()
-        for _ in range(reps):
-            out = fn()
-        return (time.perf_counter() - t) / reps, out
-
-    rng = np.random.default_rng(0)
-    lines = []
-    if "c0" in args.suite or "c1" in args.suite:
-        Xall, yall, fid = WL.onehot_ctr(60000, 0)  # one draw: 40k train / 20k test rows
-        Xtr, ytr, Xte = Xall.rows(0, 40000), yall[:40000], Xall.rows(40000, 60000)
-        ro = WL.row_orders(Xtr.n_rows, 10, 1)
-    if "c0" in args.suite:  # FM k=16, AdaGrad 0.05, batch 512, 10 epochs
-        d, k = Xtr.n_features, 16
-        V0 = rng.normal(0, 0.01, (d, k))
-
-        def fit():
-            w, V = np.zeros(d), V0.copy()
-            _rust.fm_fit_csr(Xtr.indptr, Xtr.indices, Xtr.data, d, ytr, np.ones(Xtr.n_rows), 0.0,
-                             0.0, w, V, np.zeros(d), np.zeros_like(V), "logistic", "adagrad",
-                             0.05, 1e-5, 1e-5, 0.9, 0.999, 1e-8, ro, 512, 1, 0.0, 0.0, 1.0,
-                             use_cuda=True)
-            return w, V
-        ft, (w, V) = timed(fit)
-        pt, _ = timed(lambda: _rust.fm_predict_cuda_csr(Xte.indptr, Xte.indices, Xte.data, d,
-                                                         0.0, w, V), reps=20)
-        lines.append({"suite": "c0", "model": "FM k=16 AdaGrad batch 512, 10 epochs",
-                      "train_rows": Xtr.n_rows, "fit_s": ft,
-                      "train_rows_per_s": Xtr.n_rows * 10 / ft,
-                      "predict_rows": Xte.n_rows, "predict_rows_per_s": Xte.n_rows / pt})
-    if "c1" in args.suite:  # FFM k=8, same data, field = feature // 16
-        d, F, k = Xtr.n_features, 16, 8
-        V0 = rng.uniform(0, 0.1, (d, F, k))
-
-        def fit():
-            w, V = np.zeros(d), V0.copy()
-            _rust.ffm_fit_csr(Xtr.indptr, Xtr.indices, Xtr.data, d, ytr, np.ones(Xtr.n_rows), fid,
-                              0.0, 0.0, w, V, np.zeros(d), np.zeros_like(V), "logistic",
-                              "adagrad", 0.05, 1e-5, 1e-5, 0.9, 0.999, 1e-8, ro, 512, 1, 0.0,
-                              0.0, 1.0, use_cuda=True)
-            return w, V
-        ft, (w, V) = timed(fit)
-        pt, _ = timed(lambda: _rust.ffm_predict_cuda_csr(Xte.indptr, Xte.indices, Xte.data, d,
-                                                          fid, 0.0, w, V), reps=20)
-        lines.append({"suite": "c1", "model": "FFM k=8 AdaGrad batch 512, 10 epochs",
-                      "train_rows": Xtr.n_rows, "fit_s": ft,
-                      "train_rows_per_s": Xtr.n_rows * 10 / ft,
-                      "predict_rows": Xte.n_rows, "predict_rows_per_s": Xte.n_rows / pt})
-    if "c3" in args.suite:  # FwFM k=8, FTRL (l1 1.0 / 0.1), batch 1024, 1 epoch
-        X, y, fid = WL.fwfm_ctr(200000, 3)
-        d, F, k = X.n_features, 9, 8
-        V0 = rng.normal(0, 0.01, (d, k))
-        ro3 = WL.row_orders(X.n_rows, 1, 5)
-
-        def fit():
-            w, V, r = np.zeros(d), V0.copy(), np.ones((F, F))
-            _rust.fwfm_fit_csr(X.indptr, X.indices, X.data, d, y, np.ones(X.n_rows), fid, 0.0,
-                               0.0, w, V, r, np.zeros(d), np.zeros_like(V), np.zeros((F, F)),
-                               "logistic", "ftrl", 0.05, 0.0, 0.0, 0.9, 0.999, 1e-8, ro3, 1024,
-                               1.0, 0.1, 1.0, use_cuda=True)
-            return w, V, r
-        ft, (w, V, r) = timed(fit)
-        pt, _ = timed(lambda: _rust.fwfm_predict_cuda_csr(X.indptr, X.indices, X.data, d, fid,
-                                                           0.0, w, V, r), reps=10)
-        lines.append({"suite": "c3", "model": "FwFM k=8 FTRL batch 1024, 1 epoch",
-                      "train_rows": X.n_rows, "fit_s": ft, "train_rows_per_s": X.n_rows / ft,
-                      "predict_rows": X.n_rows, "predict_rows_per_s": X.n_rows / pt})
-    if "c4" in args.suite:  # softmax FM C=10, k=8, Adam 1e-3, batch 2048, 3 epochs
-        n4 = args.suite_c4_rows
-        X, yc, sw = WL.softmax_ctr(n4, 4)
-        C, k, d = 10, 8, X.n_features
-        V0 = rng.normal(0, 0.01, (C, d, k))
-        ro4 = WL.row_orders(n4, 3, 6)
-
-        def fit():
-            w0, w, V = np.zeros(C), np.zeros((C, d)), V0.copy()
-            _rust.fm_fit_multiclass_csr(X.indptr, X.indices, X.data, d, yc, sw, w0, w, V, "adam",
-                                        1e-3, 1e-5, 1e-5, 0.1, 0.9, 0.999, 1e-8, ro4, 2048, 0.0,
-                                        0.0, 1.0, use_cuda=True)
-            return w0, w, V
-        ft, (w0, w, V) = timed(fit)
-        lines.append({"suite": "c4", "model": "softmax FM C=10 k=8 Adam batch 2048, 3 epochs",
-                      "train_rows": n4, "fit_s": ft, "train_rows_per_s": n4 * 3 / ft})
-    for ln in lines:
-        ln.update({"dtype": "f32", "path": "reference-facing API, host buffers (float64 / int64 "
-                                           "boundary format), transfers included",
-                   "data": "synthetic (seeded stand-in of the configuration)"})
-        print(json.dumps(ln), flush=True)
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1369,13 +1269,7 @@ def main():
                     choices=["float32-float64", "float32", "float64"],
                     help="compute type of the --kernel-only scoring kernel")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--suite", default="",
-                    help="comma list of the other configurations to time instead (c0,c1,c3,c4)")
-    ap.add_argument("--suite-c4-rows", type=int, default=2_000_000)
     args = ap.parse_args()
-    if args.suite:
-        run_suite(args)
-        return
     if args.impl == "reference":
         run_reference(args)
     else:
