@@ -125,34 +125,71 @@ __global__ void __launch_bounds__(kFlatNT)
     if (bad && lane == 0 && (*(volatile unsigned*)flags & bad) != bad) atomicOr(flags, bad);
 }
 
-// Sorts the row's (column << 32 | position) pairs staged in s[0, len) by a
-// bitonic network over the next power of two P >= len (padded with the
-// largest key), one warp: equal columns keep their original order (the
-// position breaks ties). O(P log^2 P / 64) steps per lane instead of the
-// O(len^2 / 32) rank loops a short row would otherwise take.
-__device__ __forceinline__ int warp_sort_row(uint64_t* s, int len, int lane) {
-    int P = 1;
-    while (P < len) P <<= 1;
-    for (int e = len + lane; e < P; e += 32) s[e] = ~0ull;
-    __syncwarp();
-    for (int k = 2; k <= P; k <<= 1)
+// Sorts a row's (column << 32 | position) pairs across one warp in registers:
+// element e = r * 32 + lane lives in v[r]; a bitonic network over 32 R keys
+// (the row's len keys, padded with the largest key), partners in other lanes
+// exchanged by shuffles and partners in other registers compared in place —
+// no shared-memory traffic. Equal columns keep their original order (the
+// position breaks ties).
+template <int R>
+__device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[R], int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32 * R; k <<= 1) {
+#pragma unroll
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = lane; i < (P >> 1); i += 32) {
-                const int a = 2 * j * (i / j) + (i % j), b = a + j;
-                const uint64_t x = s[a], y = s[b];
-                if ((x > y) == ((a & k) == 0)) {
-                    s[a] = y;
-                    s[b] = x;
+            if (j >= 32) {  // partner in register r ^ (j / 32) of the same lane
+                const int jr = j >> 5;
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    if (r & jr) continue;
+                    const int e = r * 32 + lane;
+                    const bool up = (e & k) == 0;
+                    const uint64_t x = v[r], y = v[r | jr];
+                    if ((x > y) == up) {
+                        v[r] = y;
+                        v[r | jr] = x;
+                    }
+                }
+            } else {  // partner in lane ^ j, same register
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int e = r * 32 + lane;
+                    const bool up = (e & k) == 0, lower = (lane & j) == 0;
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v[r], j);
+                    const bool keep_min = lower == up;
+                    v[r] = keep_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
                 }
             }
-            __syncwarp();
         }
-    return P;
+    }
 }
 
-__device__ __forceinline__ uint32_t sorted_col(const uint64_t* s, int e) {
-    return (uint32_t)(s[e] >> 32);
+__device__ __forceinline__ uint32_t col_of(uint64_t key) { return (uint32_t)(key >> 32); }
+
+// Sorts the row staged in s[0, len) (len <= kShortRow) and writes it back
+// sorted; registers per lane: 2 keys for rows of up to 64 entries, 8 otherwise.
+__device__ __forceinline__ void warp_sort_row(uint64_t* s, int len, int lane) {
+    if (len <= 64) {
+        uint64_t v[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : ~0ull;
+        warp_sort_regs<2>(v, lane);
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+            if (r * 32 + lane < len) s[r * 32 + lane] = v[r];
+    } else {
+        uint64_t v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : ~0ull;
+        warp_sort_regs<8>(v, lane);
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            if (r * 32 + lane < len) s[r * 32 + lane] = v[r];
+    }
+    __syncwarp();
 }
+
+__device__ __forceinline__ uint32_t sorted_col(const uint64_t* s, int e) { return col_of(s[e]); }
 
 // flags[0]: kBad* / kUnsorted bits; flags[1]: number of long unsorted rows.
 template <class T>
