@@ -64,12 +64,11 @@ struct TabArgs {
     unsigned pstep;
 };
 
-// float32 with k <= 16 under SGD / AdaGrad fits 4 blocks per SM (64 registers);
-// float64 with k <= 16 under SGD / AdaGrad 2 blocks (128 registers)
+// Blocks per SM the stage-1 kernel is held to: the per-entry column sums are
+// its largest live state (the owners' steps hold one vector at a time)
 template <class T, int NV, int OPT>
 constexpr int tab_min_blocks() {
-    return (NV <= 4 && OPT <= MFM_OPT_ADAGRAD) ? (sizeof(T) == 4 ? 4 : 2)
-                                               : (sizeof(T) == 8 && NV <= 8 && OPT <= MFM_OPT_ADAGRAD ? 2 : 1);
+    return sizeof(T) == 4 ? (NV <= 4 ? 4 : 3) : (OPT == MFM_OPT_ADAM ? 2 : 3);
 }
 
 template <class T, int VEC, int NV, int OPT>
@@ -79,6 +78,9 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
     __shared__ int wflag[NW];  // bit 0: lane 0 continues the previous warp; bit 1: one segment
     __shared__ uint32_t s_last;
     __shared__ int s_out;
+    __shared__ T s_sum[kChunk][NVAL];  // sums of the runs stepped in this block
+    __shared__ uint32_t s_key[kChunk];
+    __shared__ int s_wcnt[NW];
     const unsigned FULL = 0xffffffffu;
     pdl_trigger();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -147,62 +149,95 @@ __global__ void __launch_bounds__(kChunk, (tab_min_blocks<T, NV, OPT>())) fm_tab
     }
     __syncthreads();
     const bool owner = valid && (rhead || tid == 0);
-    if (!owner) return;
-    if (send == 31)
-        for (int w2 = warp + 1; w2 < NW; ++w2) {
-            const int f = wflag[w2];
-            if (!(f & 1)) break;
+    // mode 1: written out (a run crossing the chunk's edge leaves its partial
+    // in ph / pt; in data-parallel mode every run leaves the rank's sum in
+    // grad); 3: stepped in this block
+    int mode = 0;
+    if (owner) {
+        if (send == 31)
+            for (int w2 = warp + 1; w2 < NW; ++w2) {
+                const int f = wflag[w2];
+                if (!(f & 1)) break;
 #pragma unroll
-            for (int q = 0; q < NVAL; ++q) val[q] += wpart[w2][q];
-            if (!(f & 2)) break;
+                for (int q = 0; q < NVAL; ++q) val[q] += wpart[w2][q];
+                if (!(f & 2)) break;
+            }
+        const int64_t cb = blockIdx.x;
+        T* dst = nullptr;
+        if (tid == 0 && !rhead)
+            dst = A.ph + cb * A.TW;
+        else if (s_out && key == s_last)
+            dst = A.pt + cb * A.TW;
+        if (!dst && A.dp) dst = A.grad + (A.runs[gi] - A.run0) * A.TW;
+        if (dst) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) {
+                Vec<T, VEC> o;
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) o.v[u] = val[v * VEC + u];
+                *reinterpret_cast<Vec<T, VEC>*>(dst + v * VEC) = o;
+            }
+            dst[K] = val[K];
+            dst[K + 1] = val[K + 1];
+            mode = 1;
+        } else {
+            mode = 3;
         }
-    const int64_t cb = blockIdx.x;
-    T* dst = nullptr;
-    if (tid == 0 && !rhead)
-        dst = A.ph + cb * A.TW;
-    else if (s_out && key == s_last)
-        dst = A.pt + cb * A.TW;
-    if (dst) {
-#pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            Vec<T, VEC> o;
-#pragma unroll
-            for (int u = 0; u < VEC; ++u) o.v[u] = val[v * VEC + u];
-            *reinterpret_cast<Vec<T, VEC>*>(dst + v * VEC) = o;
-        }
-        dst[K] = val[K];
-        dst[K + 1] = val[K + 1];
-        return;
     }
-    if (A.dp) {  // the run's sum for this rank, stepped after the cross-rank sum
-        T* gd = A.grad + (A.runs[gi] - A.run0) * A.TW;
+    // the runs stepped here hand their sums to the whole block: the owners
+    // write them to shared memory in thread order, then every thread steps
+    // (run, vector) items — 16-byte parameter and state accesses of one key
+    // are taken by consecutive threads, and each thread holds one vector's
+    // state at a time
+    const unsigned m3 = __ballot_sync(FULL, mode == 3);
+    if (lane == 0) s_wcnt[warp] = __popc(m3);
+    __syncthreads();
+    int before = 0, total = 0;
 #pragma unroll
-        for (int v = 0; v < NV; ++v) {
-            Vec<T, VEC> o;
-#pragma unroll
-            for (int u = 0; u < VEC; ++u) o.v[u] = val[v * VEC + u];
-            *reinterpret_cast<Vec<T, VEC>*>(gd + v * VEC) = o;
-        }
-        gd[K] = val[K];
-        gd[K + 1] = val[K + 1];
-        return;
+    for (int w2 = 0; w2 < NW; ++w2) {
+        before += w2 < warp ? s_wcnt[w2] : 0;
+        total += s_wcnt[w2];
     }
-    // the whole run lies in this chunk: one optimizer step per coordinate
-    VecStep<T, VEC, OPT> st[NV];
+    if (mode == 3) {
+        const int slot = before + __popc(m3 & ((1u << lane) - 1u));
+#pragma unroll
+        for (int q = 0; q < NVAL; ++q) s_sum[slot][q] = val[q];
+        s_key[slot] = key;
+    }
+    __syncthreads();
+    // w of run tid; V items (run, vector) four per thread at a time, all
+    // loads of a group issued before the first step
+    const bool hw = tid < total;
     VecStep<T, 1, OPT> sw1;
+    if (hw) sw1.prefetch(A.gw, (int64_t)s_key[tid], A.opt.kind);
+    const int nvi = total * NV;
+    constexpr int G = OPT == MFM_OPT_ADAM ? 1 : OPT == MFM_OPT_FTRL ? 2 : 4;  // no spills
+    for (int base = tid; base < nvi; base += G * kChunk) {
+        VecStep<T, VEC, OPT> st[G];
 #pragma unroll
-    for (int v = 0; v < NV; ++v) st[v].prefetch(A.gv, (int64_t)key * K + v * VEC, A.opt.kind);
-    sw1.prefetch(A.gw, (int64_t)key, A.opt.kind);
+        for (int j = 0; j < G; ++j) {
+            const int it = base + j * kChunk;
+            if (it < nvi)
+                st[j].prefetch(A.gv, (int64_t)s_key[it / NV] * K + (it % NV) * VEC, A.opt.kind);
+        }
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-        T dg[VEC];
+        for (int j = 0; j < G; ++j) {
+            const int it = base + j * kChunk;
+            if (it < nvi) {  // sum gv = sum (g x S) - V sum (g x x)
+                const int slot = it / NV, v = it % NV;
+                const T* sv = s_sum[slot];
+                T dg[VEC];
 #pragma unroll
-        for (int u = 0; u < VEC; ++u)
-            dg[u] = (val[v * VEC + u] - st[v].p.v[u] * val[K + 1]) * A.inv_bsz;
-        st[v].commit(A.gv, (int64_t)key * K + v * VEC, dg, A.opt);
+                for (int u = 0; u < VEC; ++u)
+                    dg[u] = (sv[v * VEC + u] - st[j].p.v[u] * sv[K + 1]) * A.inv_bsz;
+                st[j].commit(A.gv, (int64_t)s_key[slot] * K + v * VEC, dg, A.opt);
+            }
+        }
     }
-    const T dgw = val[K] * A.inv_bsz;
-    sw1.commit(A.gw, (int64_t)key, &dgw, A.opt);
+    if (hw) {
+        const T dgw = s_sum[tid][K] * A.inv_bsz;
+        sw1.commit(A.gw, (int64_t)s_key[tid], &dgw, A.opt);
+    }
 }
 
 template <class T, int VEC, int NV>
