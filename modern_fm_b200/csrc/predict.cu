@@ -354,6 +354,39 @@ __global__ void __launch_bounds__(256)
 
 // ---------------------------------------------------------------- FwFM ----
 
+// One lane's share of a FwFM row read straight from global memory (L1-cached):
+// the lane's entries of sum w_a x_a and its pairs (a, b), a < b, taken 32
+// apart in row-major pair order with int64 cursors. The caller sums the warp.
+template <class T, class P, class IdxT, class ValT, int VEC, bool MC>
+__device__ __forceinline__ T fwfm_row_global(const IdxT* __restrict__ ix,
+                                             const ValT* __restrict__ dv, int64_t z64,
+                                             const ScoreParams<P>& M, int c, int lane) {
+    const int k = M.k, F = M.F;
+    const int C = MC ? M.C : 1;
+    T acc = T(0);
+    for (int64_t q = lane; q < z64; q += 32) acc += (T)M.w[(int64_t)ix[q] * C + c] * (T)dv[q];
+    int64_t a = 0, bb = 1 + lane;
+    while (a < z64 - 1 && bb >= z64) {
+        bb = bb - z64 + a + 2;
+        ++a;
+    }
+    while (a < z64 - 1) {
+        const IdxT ia = ix[a], ib = ix[bb];
+        const int fa = M.fid[ia], fb = M.fid[ib];
+        const int slot = fa <= fb ? fa * F + fb : fb * F + fa;  // fwfm.rs:17-21
+        const T rw = (T)M.r[(int64_t)slot * C + c];
+        const T dot = dot_global<T, P, VEC>(M.v + ((int64_t)ia * C + c) * k,
+                                            M.v + ((int64_t)ib * C + c) * k, k);
+        acc += rw * dot * (T)dv[a] * (T)dv[bb];
+        bb += 32;
+        while (a < z64 - 1 && bb >= z64) {
+            bb = bb - z64 + a + 2;
+            ++a;
+        }
+    }
+    return acc;
+}
+
 // score = w0 + sum_a w_a x_a + sum_{a<b} r[min f, max f] <v_a, v_b> x_a x_b
 // (rust/src/fwfm.rs:24-53). One warp per row; the row's latent rows (class c
 // slices) are staged in shared memory when they fit, so each is read from
@@ -425,32 +458,100 @@ __global__ void __launch_bounds__(256)
                 }
                 __syncwarp();  // sv is rewritten by the next class
             } else {
-                for (int64_t q = lane; q < z64; q += 32)
-                    acc += (T)M.w[(int64_t)ix[q] * C + c] * (T)dv[q];
-                int64_t a = 0, bb = 1 + lane;
-                while (a < z64 - 1 && bb >= z64) {
-                    bb = bb - z64 + a + 2;
-                    ++a;
-                }
-                while (a < z64 - 1) {
-                    const IdxT ia = ix[a], ib = ix[bb];
-                    const int fa = M.fid[ia], fb = M.fid[ib];
-                    const int slot = fa <= fb ? fa * F + fb : fb * F + fa;
-                    const T rw = (T)M.r[(int64_t)slot * C + c];
-                    const T dot = dot_global<T, P, VEC>(M.v + ((int64_t)ia * C + c) * k,
-                                                        M.v + ((int64_t)ib * C + c) * k, k);
-                    acc += rw * dot * (T)dv[a] * (T)dv[bb];
-                    bb += 32;
-                    while (a < z64 - 1 && bb >= z64) {
-                        bb = bb - z64 + a + 2;
-                        ++a;
-                    }
-                }
+                acc = fwfm_row_global<T, P, IdxT, ValT, VEC, MC>(ix, dv, z64, M, c, lane);
             }
             acc = warp_sum(acc);
             if (lane == 0) out[row * C + c] = (OutT)(intercept<T, MC>(M, c) + acc);
         }
         __syncwarp();
+    }
+}
+
+// Rows of at most kGroupCap entries: one group of L lanes per row (L a power
+// of two >= k), lane d owning latent dimension d. Each lane widens the row's
+// a_q = x_q v_q[d] once into registers and sums r[f_a, f_b] a_a a_b over the
+// row's pairs: one multiply-add per pair and lane, with r read from the
+// block's symmetric copy already in the arithmetic type. Rows longer than
+// kGroupCap are scored afterwards by the whole warp from global memory.
+constexpr int kGroupCap = 16;
+constexpr int kRTab = 2048;  // F * F * C entries of r held in shared memory
+
+template <class T, class P, class IdxT, class ValT, class OutT, int L, int VEC, bool MC>
+__global__ void __launch_bounds__(256, 2)
+    fwfm_group_kernel(const int64_t* __restrict__ indptr, const IdxT* __restrict__ indices,
+                      const ValT* __restrict__ data, int64_t n_rows, int64_t nnz_base,
+                      ScoreParams<P> M, OutT* __restrict__ out) {
+    constexpr int G = 32 / L;  // rows per warp pass
+    const unsigned FULL = 0xffffffffu;
+    __shared__ T s_r[kRTab];   // [c][fa][fb] = r[min, max] of class c
+    const int F = M.F, k = M.k, C = MC ? M.C : 1, FF = F * F;
+    for (int t = threadIdx.x; t < FF * C; t += blockDim.x) {
+        const int c = t / FF, q = t - c * FF, fa = q / F, fb = q - fa * F;
+        const int slot = fa <= fb ? fa * F + fb : fb * F + fa;  // fwfm.rs:17-21
+        s_r[t] = (T)M.r[(int64_t)slot * C + c];
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, d = lane & (L - 1), g = lane / L;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    for (int64_t base = warp0 * G; base < n_rows; base += nwarps * G) {
+        const int64_t row = base + g;
+        const bool live = row < n_rows;
+        int64_t b = 0, z = 0;
+        if (live) {
+            b = indptr[row] - nnz_base;
+            z = indptr[row + 1] - nnz_base - b;
+        }
+        const bool grp = live && z <= kGroupCap;
+        for (int c = 0; c < C; ++c) {
+            T acc = T(0);
+            if (grp) {
+                const IdxT* ix = indices + b;
+                const ValT* dv = data + b;
+                T a[kGroupCap];
+                int f[kGroupCap];
+#pragma unroll
+                for (int q = 0; q < kGroupCap; ++q) {
+                    a[q] = T(0);
+                    f[q] = 0;
+                    if (q < z) {
+                        const IdxT i = ix[q];
+                        const T x = (T)dv[q];
+                        f[q] = M.fid[i];
+                        if (d < k) a[q] = x * (T)M.v[((int64_t)i * C + c) * k + d];
+                        if ((q & (L - 1)) == d) acc += (T)M.w[(int64_t)i * C + c] * x;
+                    }
+                }
+                const T* rc = s_r + c * FF;
+#pragma unroll
+                for (int j = 1; j < kGroupCap; ++j) {
+                    if (j < z) {
+                        const T* rj = rc + f[j] * F;
+                        T t = T(0);
+#pragma unroll
+                        for (int i = 0; i < j; ++i) t += rj[f[i]] * a[i];
+                        acc += t * a[j];
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = L / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(FULL, acc, o);
+            if (grp && d == 0) out[row * C + c] = (OutT)(intercept<T, MC>(M, c) + acc);
+        }
+        // the pass's long rows, one at a time by the whole warp
+        unsigned longm = __ballot_sync(FULL, live && !grp && d == 0);
+        while (longm) {
+            const int64_t lrow = base + (__ffs(longm) - 1) / L;
+            longm &= longm - 1;
+            const int64_t lb = indptr[lrow] - nnz_base;
+            const int64_t lz = indptr[lrow + 1] - nnz_base - lb;
+            for (int c = 0; c < C; ++c) {
+                T acc = fwfm_row_global<T, P, IdxT, ValT, VEC, MC>(indices + lb, data + lb, lz, M,
+                                                                   c, lane);
+                acc = warp_sum(acc);
+                if (lane == 0) out[lrow * C + c] = (OutT)(intercept<T, MC>(M, c) + acc);
+            }
+        }
     }
 }
 
@@ -587,8 +688,34 @@ void fwfm_launch(int device, cudaStream_t s, const int64_t* indptr, const IdxT* 
                  const ValT* data, int64_t n_rows, int64_t nnz_base, const ScoreParams<P>& M,
                  OutT* out) {
     if (n_rows <= 0) return;
-    const unsigned grid = warp_grid(device, n_rows, kWarps, kBlocksPerSm);
     const int vw = vec_width<P>(M.k, M.v);
+    const int64_t rtab = (int64_t)M.F * M.F * (MC ? M.C : 1);
+    if (M.k <= 32 && rtab <= kRTab) {
+        const int L = M.k <= 4 ? 4 : M.k <= 8 ? 8 : M.k <= 16 ? 16 : 32;
+        const unsigned grid = warp_grid(device, ceil_div(n_rows, (int64_t)(32 / L)), kWarps,
+                                        kBlocksPerSm);
+#define MFM_FWFM_GROUP(LL, VV)                                                                  \
+    fwfm_group_kernel<T, P, IdxT, ValT, OutT, LL, VV, MC>                                      \
+        <<<grid, kWarps * 32, 0, s>>>(indptr, indices, data, n_rows, nnz_base, M, out)
+#define MFM_FWFM_L(LL)                                                                          \
+    if (L == LL) {                                                                              \
+        if (vw == 4)                                                                            \
+            MFM_FWFM_GROUP(LL, (16 / sizeof(P) >= 4 ? 4 : 1));                                  \
+        else if (vw == 2)                                                                       \
+            MFM_FWFM_GROUP(LL, 2);                                                              \
+        else                                                                                    \
+            MFM_FWFM_GROUP(LL, 1);                                                              \
+    }
+        MFM_FWFM_L(4)
+        MFM_FWFM_L(8)
+        MFM_FWFM_L(16)
+        MFM_FWFM_L(32)
+#undef MFM_FWFM_L
+#undef MFM_FWFM_GROUP
+        MFM_CHECK_LAUNCH("FwFM predict launch");
+        return;
+    }
+    const unsigned grid = warp_grid(device, n_rows, kWarps, kBlocksPerSm);
     if (vw == 4)
         fwfm_predict_kernel<T, P, IdxT, ValT, OutT, (16 / sizeof(P) >= 4 ? 4 : 1), MC>
             <<<grid, kWarps * 32, 0, s>>>(indptr, indices, data, n_rows, nnz_base, M, out);

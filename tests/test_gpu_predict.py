@@ -187,6 +187,38 @@ def test_known_answers():
     assert abs(out[0] - 9.5) < 1e-12
 
 
+@pytest.mark.parametrize("k", [1, 3, 4, 5, 8, 16, 17, 32, 33])
+@pytest.mark.parametrize("F", [3, 9, 46])
+@pytest.mark.parametrize("dtype", ["float64", "float32"])
+def test_fwfm_row_lengths_latent_widths_and_field_counts(k, F, dtype, monkeypatch):
+    """FwFM rows of every length 0..40 in one call (the register-staged rows
+    of at most 16 entries and the longer ones scored by a whole warp), latent
+    widths on both sides of each lane-group size, and a field count whose
+    F x F table is too large for the block's shared copy (46 x 46)."""
+    monkeypatch.setenv("MFM_B200_DTYPE", dtype)
+    rng = np.random.default_rng(1000 * k + F)
+    d = 300
+    lens = np.tile(np.arange(41), 3)
+    rng.shuffle(lens)
+    ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    ix = np.concatenate([np.sort(rng.choice(d, size=n, replace=False)) for n in lens])
+    ix = ix.astype(np.int64)
+    dv = rng.uniform(-1.0, 1.0, size=len(ix))
+    fid = rng.integers(0, F, size=d)
+    w0, w = 0.25, rng.normal(size=d) * 0.3
+    V, r = rng.normal(size=(d, k)) * 0.3, rng.uniform(size=(F, F))
+    if dtype == "float32":
+        w, V, r = (a.astype(np.float32).astype(np.float64) for a in (w, V, r))
+    got = _rust.fwfm_predict_cuda_csr(ip, ix, dv, d, fid, w0, w, V, r)
+    want = O.fwfm_predict_csr(ip, ix, dv, d, fid, w0, w, V, r)
+    if dtype == "float64":
+        np.testing.assert_allclose(got, want, rtol=RTOL64, atol=ATOL64)
+    else:
+        scale = O.fwfm_predict_csr(ip, ix, np.abs(dv), d, fid, w0, np.abs(w), np.abs(V),
+                                   r) + 1.0
+        assert np.all(np.abs(got - want) <= RTOL32 * np.abs(want) + 1e-5 * scale)
+
+
 def test_ffm_large_row(f64):
     # a single row with z = 2048 nonzeros (tests/test_cuda_parity.py:126-136)
     rng = np.random.default_rng(0)
