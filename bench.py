@@ -429,10 +429,13 @@ def train_measure(args, rank, world, local, dev_t, L, _lib):
 
 
 def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
-    """One data-parallel fit across all ranks (N > 1): the same 10M-row epoch,
-    every global batch of 4096 rows split over the ranks, one allreduce of the
-    batch's per-key gradient sums per batch, in float64. Parity: rank 0 also
-    fits the same epochs on its own GPU alone and compares."""
+    """One data-parallel fit across all ranks (N > 1): the same 10M-row epoch
+    and global batches of 4096 rows, in float64, parameter-sharded by key
+    (each rank owns 1/N of the keys and their optimizer state, scores every
+    row over its own keys, and the ranks sum the batch's row table, 4096 x
+    (k + 2) values, with one NCCL allreduce per batch; the engine's default).
+    Parity: rank 0 also fits the same epochs on its own GPU alone and
+    compares."""
     import torch
 
     from modern_fm_b200 import dp as DP
@@ -485,8 +488,8 @@ def train_dp_measure(args, rank, world, local, dev_t, L, _lib):
     barrier(world)
     if rank != 0:
         return None
-    return {"metric": "FM AdaGrad data-parallel training rows/s (one fit, global batch 4096 "
-                      "split over the ranks, NCCL allreduce per batch)",
+    return {"metric": "FM AdaGrad data-parallel training rows/s (one fit, global batch 4096, "
+                      "parameters sharded by key, NCCL allreduce of the row table per batch)",
             "value": n / (ms / 1e3), "unit": "rows/s", "n_gpus": world, "rows": n,
             "dtype": "f64", "steps": args.train_steps, "ms_per_step": ms, "scaling": "strong",
             "batches_ms_per_epoch": batches_ms, "parity": parity}

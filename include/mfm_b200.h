@@ -361,13 +361,26 @@ int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr, const int32_
                       mfm_dev_group* v, void* stream);
 
 /* ---- data-parallel training (no reference counterpart) -------------------
- * Synchronous data parallelism over NCCL (NVLink / NVSwitch): every rank holds
- * the whole training set, the parameters and the optimizer state; each global
- * batch (the same row_orders chunking as one GPU) is cut into `world`
- * contiguous row slices, rank r scores slice r, the per-key gradient sums over
- * the batch's sorted union of touched keys are summed across ranks with one
- * ncclAllReduce, and every rank applies the identical optimizer step. NCCL is
- * loaded on first use (dlopen "libnccl.so.2").
+ * Synchronous multi-GPU training with the one-GPU mini-batch semantics (the
+ * same row_orders chunking, every batch's step equal to a one-GPU step up to
+ * summation order); every rank holds the whole training set. Two exchanges:
+ *   binary FM with k = 2, 4, 8, 16 (float64) or 4, 8, 16, 32 (float32), the
+ *     row-table path: parameter-sharded by key. Rank r owns the keys with
+ *     key mod world = r (parameters and optimizer state stepped there only)
+ *     and scores every row of each batch over its own keys; the ranks sum
+ *     the batch's row table (rows x (k + 1) values) with one ncclAllReduce
+ *     (or, with MFM_B200_DP_EXCHANGE=peer, the forward kernel reads the other
+ *     ranks' rows over NVLink through CUDA IPC mappings, with bounded flag
+ *     waits); after the fit one sum over the ranks gives every rank every
+ *     key. MFM_B200_DP_MODE=runs selects the second exchange instead;
+ *   every other shape (FFM, FwFM, multiclass, other k): parameters
+ *     replicated; each global batch is cut into `world` contiguous row
+ *     slices, rank r scores slice r, the per-key gradient sums over the
+ *     batch's sorted union of touched keys are summed with one
+ *     ncclAllReduce, and every rank applies the identical optimizer step.
+ * NCCL is loaded on first use (dlopen "libnccl.so.2"). A rank that stops
+ * answering ends the other ranks' fits with an error after
+ * MFM_B200_DP_TIMEOUT seconds (default 300); the group must then be recreated.
  *   mfm_dp_unique_id: rank 0 makes the group id (128 bytes) and the caller
  *     hands it to every rank;
  *   mfm_dp_create: every rank, concurrently; binds the group to `device`;
@@ -378,8 +391,8 @@ int mfm_dp_create(const unsigned char id[128], int world, int rank, int device, 
 int mfm_dp_destroy(mfm_dp* dp);
 
 /* mfm_fm_fit_device across the group (same arguments; the device is the
- * group's). Every rank must call it with the same data, row orders and
- * hyperparameters; results are identical on every rank. */
+ * group's). Every rank must call it with the same data, row orders, initial
+ * parameters and hyperparameters; results are identical on every rank. */
 int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr, const int32_t* indices,
                          const void* data, int64_t n_rows, int64_t n_features, const void* y,
                          const void* sample_weight, const int32_t* row_orders,
@@ -394,12 +407,10 @@ int mfm_fm_fit_device_dp(mfm_dp* dp, int dtype, const int64_t* indptr, const int
  * mfm_ffm_fit_csr / mfm_ffm_fit_multiclass_csr / mfm_fwfm_fit_csr /
  * mfm_fwfm_fit_multiclass_csr on the group's device (field_ids / n_fields for
  * FFM and FwFM, r for FwFM; NULL otherwise). Every rank calls it with the
- * same data, row orders, initial parameters and hyperparameters; each global
- * batch's rows are split into `world` contiguous slices, each rank's gradient
- * sums over the batch's touched keys are summed across ranks (NCCL), and every
- * rank applies the identical step, so every rank ends with the same
- * parameters, equal to a one-GPU fit up to summation order. No reference
- * counterpart (the reference trains on one device). */
+ * same data, row orders, initial parameters and hyperparameters (either
+ * exchange above, by shape), so every rank ends with the same parameters,
+ * equal to a one-GPU fit up to summation order. No reference counterpart (the
+ * reference trains on one device). */
 int mfm_fit_csr_dp(mfm_dp* dp, int dtype, int model, int64_t n_classes, const mfm_csr* x,
                    const double* y, const int64_t* ycls, const double* sample_weight,
                    const int64_t* field_ids, int64_t n_fields, const mfm_train* tr, int64_t k,

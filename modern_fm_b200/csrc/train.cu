@@ -39,16 +39,28 @@
 #include <cmath>
 
 #include "train_tab.cuh"
+#include "train_shard.cuh"
+#include "scan.cuh"
 
 // A data-parallel group: one NCCL communicator bound to a device.
 struct mfm_dp {
     ncclComm_t comm;
     int world, rank, device;
-    // batches whose cross-rank sum has completed, written by the device into
-    // mapped host memory (the host's liveness view of the group)
+    // mapped host words written by the device: [0] batches whose cross-rank
+    // sum has completed (the host's liveness view of the group), [1] set when
+    // a wait for a peer's flag gave up
     unsigned* prog_h;
     unsigned* prog_d;
     bool aborted;  // the communicator was aborted after a failure
+    // Peer-memory exchange: one device buffer per rank, exported by CUDA IPC
+    // and mapped by every other rank: a flag area (the rank's exchange count,
+    // a failure word), then the exchange data. seq counts the group's
+    // exchanges (the same on every rank; flags hold it, so they never reset).
+    void* sym = nullptr;
+    size_t sym_bytes = 0;
+    std::vector<void*> peer;  // every rank's buffer as mapped here (own at [rank])
+    unsigned long long seq = 0;
+    int p2p = -1;  // -1 not set up, 0 unavailable (NCCL exchange), 1 mapped
 };
 
 namespace mfm {
@@ -146,6 +158,10 @@ struct NcclApi {
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*Broadcast)(const void*, void*, size_t, ncclDataType_t, int, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
 };
 inline const NcclApi& nccl() {
     static const NcclApi api = [] {
@@ -162,11 +178,13 @@ inline const NcclApi& nccl() {
         a.GetErrorString = (decltype(a.GetErrorString))dlsym(h, "ncclGetErrorString");
         a.GroupStart = (decltype(a.GroupStart))dlsym(h, "ncclGroupStart");
         a.GroupEnd = (decltype(a.GroupEnd))dlsym(h, "ncclGroupEnd");
+        a.Broadcast = (decltype(a.Broadcast))dlsym(h, "ncclBroadcast");
+        a.AllGather = (decltype(a.AllGather))dlsym(h, "ncclAllGather");
         return a;
     }();
     if (!api.GetUniqueId || !api.CommInitRank || !api.AllReduce || !api.CommDestroy ||
         !api.CommAbort || !api.CommGetAsyncError || !api.GetErrorString || !api.GroupStart ||
-        !api.GroupEnd)
+        !api.GroupEnd || !api.Broadcast || !api.AllGather)
         fail(MFM_ERR_UNSUPPORTED, "NCCL (libnccl.so.2) could not be loaded");
     return api;
 }
@@ -179,6 +197,147 @@ inline const NcclApi& nccl() {
 
 // Data-parallel: batches the host may enqueue ahead of the device's progress.
 constexpr uint32_t kDpAhead = 64;
+
+// The group's liveness limit in seconds (MFM_B200_DP_TIMEOUT, default 300).
+inline double dp_timeout_s() {
+    static const double limit = [] {
+        const char* e = getenv("MFM_B200_DP_TIMEOUT");
+        const double v = e ? atof(e) : 0.0;
+        return v > 0.0 ? v : 300.0;
+    }();
+    return limit;
+}
+
+// Waits for stream s under the group's liveness rules: a group error reported
+// by NCCL, or no completion within the limit, aborts the communicator, lets
+// the stream drain and fails the call.
+inline void dp_sync(mfm_dp* dp, cudaStream_t s, const char* what) {
+    const double limit = dp_timeout_s();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) return;
+        if (q != cudaErrorNotReady) MFM_CUDA(q, what);
+        ncclResult_t st = ncclSuccess;
+        nccl().CommGetAsyncError(dp->comm, &st);
+        const bool failed = st != ncclSuccess && st != ncclInProgress;
+        if (failed ||
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit) {
+            nccl().CommAbort(dp->comm);
+            dp->aborted = true;
+            cudaStreamSynchronize(s);  // the aborted collective lets the stream drain
+            if (failed)
+                fail(MFM_ERR_CUDA, fmt("data-parallel group failed in %s (NCCL: %s); the group "
+                                       "was aborted",
+                                       what, nccl().GetErrorString(st)));
+            fail(MFM_ERR_CUDA, fmt("data-parallel group: %s did not complete in %.0f s (a peer "
+                                   "is not answering); the group was aborted",
+                                   what, limit));
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+}
+
+// One NCCL allreduce (min) of an int across the group.
+inline int dp_all_min(mfm_dp* dp, int v, cudaStream_t s) {
+    DevBuf<int> b(dp->device, 1);
+    h2d(b.ptr, &v, 1, s, "group agreement");
+    const ncclResult_t r = nccl().AllReduce(b.ptr, b.ptr, 1, ncclInt32, ncclMin, dp->comm, s);
+    if (r != ncclSuccess) {
+        nccl().CommAbort(dp->comm);
+        dp->aborted = true;
+        cudaStreamSynchronize(s);
+        fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group was aborted",
+                               nccl().GetErrorString(r)));
+    }
+    int out = 0;
+    d2h(&out, b.ptr, 1, s, "group agreement");
+    dp_sync(dp, s, "the group agreement");
+    return out;
+}
+
+// Unmaps the peers' exchange buffers and frees this rank's, after every rank
+// has unmapped (collective unless the group was aborted).
+inline void dp_sym_release(mfm_dp* dp, cudaStream_t s) {
+    if (!dp->sym) return;
+    for (int p = 0; p < (int)dp->peer.size(); ++p)
+        if (p != dp->rank && dp->peer[p]) cudaIpcCloseMemHandle(dp->peer[p]);
+    dp->peer.clear();
+    if (!dp->aborted) dp_all_min(dp, 1, s);
+    cudaFree(dp->sym);
+    dp->sym = nullptr;
+    dp->sym_bytes = 0;
+    dp->p2p = -1;
+}
+
+// Sets up (or grows) the peer-memory exchange: every rank allocates `need`
+// bytes (zeroed), exports them by CUDA IPC and maps every other rank's.
+// p2p = 1 when every rank mapped every peer; otherwise 0 and the exchange
+// goes through NCCL. Opt-in: MFM_B200_DP_EXCHANGE=peer (the NCCL exchange
+// is the default: on 2 B200s it measured faster, 108 against 113 ms per
+// 10M-row epoch). Collective: every rank calls it with the same size.
+inline void dp_sym_ensure(mfm_dp* dp, size_t need, cudaStream_t s) {
+    if (dp->p2p == 0) return;
+    if (dp->p2p == 1 && dp->sym_bytes >= need) return;
+    const char* e = getenv("MFM_B200_DP_EXCHANGE");
+    if (!(e && strcmp(e, "peer") == 0) || dp->world > kMaxDpRanks) {
+        dp->p2p = 0;
+        return;
+    }
+    dp_sym_release(dp, s);
+    MFM_CUDA(cudaMalloc(&dp->sym, need), "exchange buffer");
+    dp->sym_bytes = need;
+    MFM_CUDA(cudaMemsetAsync(dp->sym, 0, need, s), "exchange buffer");
+    struct Rec {
+        cudaIpcMemHandle_t h;
+        int dev, ok;
+        char pad[56];
+    };
+    static_assert(sizeof(Rec) == 128, "exchange record");
+    Rec mine;
+    memset(&mine, 0, sizeof(mine));
+    mine.ok = cudaIpcGetMemHandle(&mine.h, dp->sym) == cudaSuccess ? 1 : 0;
+    cudaGetLastError();
+    mine.dev = dp->device;
+    const int W = dp->world;
+    DevBuf<char> recs(dp->device, (int64_t)W * sizeof(Rec));
+    h2d(recs.ptr + (size_t)dp->rank * sizeof(Rec), reinterpret_cast<const char*>(&mine),
+        sizeof(Rec), s, "exchange handles");
+    const ncclResult_t r = nccl().AllGather(recs.ptr + (size_t)dp->rank * sizeof(Rec), recs.ptr,
+                                            sizeof(Rec), ncclChar, dp->comm, s);
+    if (r != ncclSuccess) {
+        nccl().CommAbort(dp->comm);
+        dp->aborted = true;
+        cudaStreamSynchronize(s);
+        fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group was aborted",
+                               nccl().GetErrorString(r)));
+    }
+    std::vector<Rec> all(W);
+    d2h(reinterpret_cast<char*>(all.data()), recs.ptr, (size_t)W * sizeof(Rec), s,
+        "exchange handles");
+    dp_sync(dp, s, "the exchange set-up");
+    dp->peer.assign(W, nullptr);
+    dp->peer[dp->rank] = dp->sym;
+    int ok = 1;
+    for (int p = 0; p < W; ++p) ok &= all[p].ok;
+    for (int p = 0; p < W && ok; ++p) {
+        if (p == dp->rank) continue;
+        int can = 0;
+        if (cudaDeviceCanAccessPeer(&can, dp->device, all[p].dev) != cudaSuccess || !can ||
+            cudaIpcOpenMemHandle(&dp->peer[p], all[p].h, cudaIpcMemLazyEnablePeerAccess) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            dp->peer[p] = nullptr;
+            ok = 0;
+        }
+    }
+    if (dp_all_min(dp, ok, s)) {
+        dp->p2p = 1;
+    } else {
+        dp_sym_release(dp, s);
+        dp->p2p = 0;
+    }
+}
 
 struct Events {
     std::vector<cudaEvent_t> e;
@@ -268,6 +427,16 @@ struct Trainer {
     DevBuf<GridBar> bar;
     bool coop = false;  // cooperative launches usable (persistent epoch loop)
     mfm_dp* dp = nullptr;  // data-parallel group (row-table path only)
+    // parameter-sharded data-parallel training (binary FM row-table path):
+    // this rank's keys (key mod world = rank), its restriction of the CSR, and the
+    // partial row table that the group sums every batch (stride PW)
+    bool shard = false;
+    int64_t sh_rows = 0;
+    DevBuf<int64_t> sh_indptr;
+    DevBuf<int32_t> sh_indices;
+    DevBuf<T> sh_data, part;
+    DevBuf<ShardXchDev> sh_xch;  // the peer exchange's buffers, as the device sees them
+    int PW = 0;
 
     void upload_group(int gi, const mfm_group* hg, int64_t R, int64_t K, int reg) {
         const int64_t n = (int64_t)C * R * K;
@@ -683,6 +852,17 @@ struct Trainer {
         }
     }
 
+    // grid capped to the blocks that are resident at once (kernels whose
+    // blocks wait on the same blocks of other ranks)
+    template <class K>
+    unsigned resident_cap(K kern, unsigned grid) {
+        int per_sm = 0;
+        MFM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0),
+                 "occupancy");
+        const int64_t cap = std::min<int64_t>((int64_t)per_sm * sm_count(device), kDpMaxBlocks);
+        if (cap < 1) fail(MFM_ERR_CUDA, "the exchange kernel cannot be resident");
+        return (unsigned)std::min<int64_t>(grid, cap);
+    }
     void launch_forward(const FwdArgs<T>& A, int64_t nrows) {
         const unsigned grid = warp_grid(device, nrows, 8, 8);
         if (model == M_FM && !multiclass) {
@@ -694,7 +874,13 @@ struct Trainer {
     {                                                                                       \
         const int64_t want = ceil_div(nrows * LR_, 256);                                    \
         const unsigned gr = (unsigned)std::max<int64_t>(1, std::min<int64_t>(g, want));     \
-        if (S[0].tab)                                                                       \
+        if (S[0].tab && shard)                                                              \
+            launch_pdl(fm_forward_rows_kernel<T, VW, L_, LR_, CAP_, true, true>,              \
+                       A.xch ? resident_cap(fm_forward_rows_kernel<T, VW, L_, LR_, CAP_, true, \
+                                                                   true>, gr)                \
+                             : gr,                                                          \
+                       256, s, A);                                                          \
+        else if (S[0].tab)                                                                  \
             launch_pdl(fm_forward_rows_kernel<T, VW, L_, LR_, CAP_, true>, gr, 256, s, A);  \
         else                                                                                \
             fm_forward_rows_kernel<T, VW, L_, LR_, CAP_><<<gr, 256, 0, s>>>(A);             \
@@ -830,15 +1016,16 @@ struct Trainer {
         TA.gw = G[1];
         TA.gw0 = G[0];
         TA.opt = opt;
-        TA.dp = dp ? 1 : 0;
+        const bool runs = dp && !shard;  // the run-sum exchange
+        TA.dp = runs ? 1 : 0;
         TA.rlo = (uint32_t)rlo;
         TA.rhi = (uint32_t)rhi;
         TA.runs = st_.runs.ptr;
         TA.rkey = st_.rkey.ptr;
-        TA.run0 = dp ? st_.h_run[b] : 0;
-        TA.nrun = dp ? st_.h_run[b + 1] - st_.h_run[b] : 0;
+        TA.run0 = runs ? st_.h_run[b] : 0;
+        TA.nrun = runs ? st_.h_run[b + 1] - st_.h_run[b] : 0;
         TA.grad = st_.grad.ptr;
-        TA.progress = dp ? dp->prog_d : nullptr;
+        TA.progress = runs ? dp->prog_d : nullptr;
         TA.pstep = step;
         for (auto& r : TA.pre) r = L2Range{nullptr, 0};
         if (b + 1 < nb) {  // the next batch's epoch-order rows, pulled into L2 by stage 2
@@ -977,15 +1164,20 @@ struct Trainer {
     // by NCCL, or no progress for MFM_B200_DP_TIMEOUT seconds (default 300),
     // aborts the communicator, lets the stream drain and fails the call.
     void dp_wait(uint32_t target) {
-        static const double limit = [] {
-            const char* e = getenv("MFM_B200_DP_TIMEOUT");
-            const double v = e ? atof(e) : 0.0;
-            return v > 0.0 ? v : 300.0;
-        }();
+        const double limit = dp_timeout_s();
         volatile unsigned* p = dp->prog_h;
         unsigned last = *p;
         auto t_last = std::chrono::steady_clock::now();
         while ((int32_t)(*p - target) < 0) {
+            if (p[1]) {  // a peer-memory exchange gave up waiting for a peer
+                nccl().CommAbort(dp->comm);
+                dp->aborted = true;
+                cudaStreamSynchronize(s);  // the exchange kernels return on their own
+                fail(MFM_ERR_CUDA, fmt("data-parallel group: a peer did not publish its batch "
+                                       "within %.0f s (a peer is not answering); the group was "
+                                       "aborted",
+                                       limit));
+            }
             ncclResult_t st = ncclSuccess;
             nccl().CommGetAsyncError(dp->comm, &st);
             const unsigned cur = *p;
@@ -1055,7 +1247,7 @@ struct Trainer {
                     plan_tab_window(S[0], (int)e, win[w].first, win[w].second, lo);
                     MFM_CUDA(cudaEventRecord(ev.e[w], lo), "event");
                 }
-                if (dp) plan_tab_runs(S[0]);
+                if (dp && !shard) plan_tab_runs(S[0]);
                 for (size_t w = 0; w < win.size(); ++w) {
                     MFM_CUDA(cudaStreamWaitEvent(hi, ev.e[w], 0), "event");
                     for (int64_t b = win[w].first; b < win[w].second; ++b) {
@@ -1066,13 +1258,23 @@ struct Trainer {
                         if (dp && gstep > kDpAhead) dp_wait(gstep - kDpAhead);
                         const int64_t pos0 = b * B, nrows = std::min(B, n_rows - pos0);
                         const T inv_bsz = T(1) / (T)nrows;  // batch length (fm.rs:395-398)
-                        // data-parallel: this rank scores rows [rlo, rhi) of the batch
-                        const int64_t rlo = dp ? nrows * dp->rank / dp->world : 0;
-                        const int64_t rhi = dp ? nrows * (dp->rank + 1) / dp->world : nrows;
+                        // data-parallel (run sums): this rank scores rows [rlo, rhi)
+                        // of the batch; sharded: every row, over the rank's keys
+                        const bool slice = dp && !shard;
+                        const int64_t rlo = slice ? nrows * dp->rank / dp->world : 0;
+                        const int64_t rhi = slice ? nrows * (dp->rank + 1) / dp->world : nrows;
                         FwdArgs<T> A = base;
                         A.pos0 = pos0 + rlo;
                         A.nrows = rhi - rlo;
-                        A.tab = base.tab + rlo * base.TW;
+                        const unsigned long long seq = shard ? ++dp->seq : 0;
+                        A.tab = shard ? shard_part(seq) : base.tab + rlo * base.TW;
+                        if (shard && dp->p2p == 1) {  // the forward runs the exchange
+                            A.xch = sh_xch.ptr;
+                            A.seq = seq;
+                            A.tab_out = S[0].table.ptr;
+                            A.step = gstep;
+                        }
+                        A.TW = shard ? PW : base.TW;
                         A.grow = base.grow + rlo;
                         A.indptr = S[0].estart.ptr;  // rows by epoch position
                         A.indices = reinterpret_cast<const int32_t*>(S[0].pidx.ptr);
@@ -1086,6 +1288,7 @@ struct Trainer {
                             A.pre[2] = L2Range{S[0].rx.ptr + sg, ne * (int64_t)sizeof(T)};
                         }
                         launch_forward(A, rhi - rlo);
+                        if (shard) shard_exchange(pos0, nrows, gstep);
                         launch_tab(b, inv_bsz, nrows, rlo, rhi, gstep);
                     }
                 }
@@ -1151,9 +1354,136 @@ struct Trainer {
         MFM_CHECK_LAUNCH("data-parallel apply");
     }
 
+    // Parameter-sharded data parallelism (the row-table path's default;
+    // MFM_B200_DP_MODE=runs selects the exchange of per-key run sums instead):
+    // this rank's keys and its restriction of the CSR, which the plan and the
+    // forward then see in place of the whole CSR.
+    static bool shard_mode() {
+        const char* m = getenv("MFM_B200_DP_MODE");
+        return !(m && strcmp(m, "runs") == 0);
+    }
+    void shard_setup() {
+        constexpr int VW = 16 / (int)sizeof(T);
+        const int N = dp->world, r = dp->rank;
+        DevBuf<int64_t> cnt(device, std::max<int64_t>(1, n_rows));
+        const unsigned g = warp_grid(device, n_rows, 8, 8);
+        shard_count_kernel<<<g, 256, 0, s>>>(p_indptr, p_indices, n_rows, N, r, cnt.ptr);
+        sh_indptr.alloc(device, n_rows + 1);
+        exclusive_scan<int64_t, int64_t>(device, s, cnt.ptr, n_rows, sh_indptr.ptr);
+        int64_t nnz = 0;
+        d2h(&nnz, sh_indptr.ptr + n_rows, 1, s, "shard plan");
+        MFM_CUDA(cudaStreamSynchronize(s), "shard plan");
+        sh_indices.alloc(device, std::max<int64_t>(1, nnz));
+        sh_data.alloc(device, std::max<int64_t>(1, nnz));
+        shard_copy_kernel<T><<<g, 256, 0, s>>>(p_indptr, p_indices, p_data, n_rows, N, r,
+                                               sh_indptr.ptr, sh_indices.ptr, sh_data.ptr);
+        MFM_CHECK_LAUNCH("shard plan");
+        p_indptr = sh_indptr.ptr;
+        p_indices = sh_indices.ptr;
+        p_data = sh_data.ptr;
+        PW = (int)k + VW;  // [S | lin - sq / 2], padded to a 16-byte row
+        sh_rows = std::max<int64_t>(1, std::min(B, n_rows));
+        // peer-memory exchange: two partial tables (alternating by batch)
+        dp_sym_ensure(dp, kDpDataOffset + 2 * (size_t)sh_rows * PW * sizeof(T), s);
+        if (dp->p2p == 1) {
+            ShardXchDev X{};
+            for (int p = 0; p < dp->world; ++p) {
+                const char* base = static_cast<const char*>(dp->peer[p]);
+                for (int par = 0; par < 2; ++par)
+                    X.part[par][p] = base + kDpDataOffset + (size_t)par * sh_rows * PW * sizeof(T);
+                X.flags[p] = reinterpret_cast<const unsigned long long*>(base + kDpFlagsOffset);
+            }
+            X.my_flags = reinterpret_cast<unsigned long long*>(static_cast<char*>(dp->sym) +
+                                                               kDpFlagsOffset);
+            X.fail = static_cast<unsigned*>(dp->sym);
+            X.fail_h = dp->prog_d + 1;
+            X.progress = dp->prog_d;
+            X.spin = (unsigned long long)(dp_timeout_s() * 5e6);
+            X.N = dp->world;
+            X.rank = dp->rank;
+            X.PW = PW;
+            sh_xch.alloc(device, 1);
+            h2d(sh_xch.ptr, &X, 1, s, "exchange set-up");
+            MFM_CUDA(cudaStreamSynchronize(s), "exchange set-up");
+        } else {
+            part.alloc(device, sh_rows * PW);
+        }
+        shard = true;
+    }
+    // This rank's partial table for exchange number seq.
+    T* shard_part(unsigned long long seq) {
+        if (dp->p2p != 1) return part.ptr;
+        return reinterpret_cast<T*>(static_cast<char*>(dp->sym) + kDpDataOffset) +
+               (int64_t)(seq & 1) * sh_rows * PW;
+    }
+    // NCCL failure inside the fit: abort the communicator, let the stream
+    // drain, fail the call.
+    [[noreturn]] void dp_failed(ncclResult_t r) {
+        nccl().CommAbort(dp->comm);
+        dp->aborted = true;
+        cudaStreamSynchronize(s);
+        fail(MFM_ERR_CUDA, fmt("data-parallel group failed (NCCL: %s); the group was aborted",
+                               nccl().GetErrorString(r)));
+    }
+    // Batch rows [pos0, pos0 + nrows) after the forward: the group's sum of
+    // the partial row table, then S, the scores and g (identical on every rank).
+    void shard_exchange(int64_t pos0, int64_t nrows, uint32_t step) {
+        constexpr int VW = 16 / (int)sizeof(T);
+        MFM_CHECK_LAUNCH("FM forward");
+        if (dp->p2p == 1) return;  // the forward exchanged and finished its rows
+        const ncclResult_t r =
+            nccl().AllReduce(part.ptr, part.ptr, (size_t)(nrows * PW),
+                             sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum, dp->comm, s);
+        if (r != ncclSuccess) dp_failed(r);  // e.g. a peer process exited
+        const unsigned g = (unsigned)std::max<int64_t>(1, ceil_div(nrows, 256));
+#define MFM_FINISH(NV_)                                                                     \
+    fm_shard_finish_kernel<T, VW, NV_><<<g, 256, 0, s>>>(                                   \
+        part.ptr, PW, S[0].table.ptr, grow.ptr, S[0].py.ptr, S[0].psw.ptr, pos0, nrows, G[0].p, \
+        tr->loss, dp->prog_d, step)
+        switch (k / VW) {
+        case 1: MFM_FINISH(1); break;
+        case 2: MFM_FINISH(2); break;
+        case 4: MFM_FINISH(4); break;
+        default: MFM_FINISH(8); break;
+        }
+#undef MFM_FINISH
+        MFM_CHECK_LAUNCH("shard exchange");
+    }
+    // After the fit: every rank zeroes the keys it does not own (parameters
+    // and optimizer state) and one sum over the ranks gives every rank the
+    // owners' values.
+    void shard_gather() {
+        for (int gi = 1; gi <= 2; ++gi) {
+            const GroupDev<T>& g = G[gi];
+            T* arrs[7] = {g.p, g.acc, g.m, g.s, g.t, g.z, g.n};
+            for (T* a : arrs)
+                if (a)
+                    shard_zero_unowned_kernel<T><<<blocks_for(n_feat * g.width, 256), 256, 0,
+                                                   s>>>(a, n_feat, g.width, dp->world,
+                                                        dp->rank);
+        }
+        MFM_CHECK_LAUNCH("shard gather");
+        ncclResult_t r = nccl().GroupStart();
+        for (int gi = 1; gi <= 2 && r == ncclSuccess; ++gi) {
+            const GroupDev<T>& g = G[gi];
+            T* arrs[7] = {g.p, g.acc, g.m, g.s, g.t, g.z, g.n};
+            for (T* a : arrs)
+                if (a && r == ncclSuccess)
+                    r = nccl().AllReduce(a, a, (size_t)(n_feat * g.width),
+                                         sizeof(T) == 4 ? ncclFloat32 : ncclFloat64, ncclSum,
+                                         dp->comm, s);
+        }
+        const ncclResult_t r2 = nccl().GroupEnd();
+        if (r == ncclSuccess) r = r2;
+        if (r != ncclSuccess) dp_failed(r);
+        dp_sync(dp, s, "the final gather");
+    }
+
     void run(const FwdArgs<T>& base, PhaseTimer& pt) {
         if (S[0].tab) {
+            if (dp && shard_mode()) shard_setup();
             run_tab(base, pt);
+            if (shard) shard_gather();
             return;
         }
         uint32_t gstep = 0;  // batches enqueued in this call (data-parallel liveness)
@@ -1576,8 +1906,8 @@ extern "C" int mfm_dp_create(const unsigned char id[128], int world, int rank, i
         memcpy(&u, id, sizeof(u));
         unsigned* h = nullptr;
         unsigned* dptr = nullptr;
-        MFM_CUDA(cudaHostAlloc(&h, sizeof(unsigned), cudaHostAllocMapped), "progress word");
-        *h = 0u;
+        MFM_CUDA(cudaHostAlloc(&h, 2 * sizeof(unsigned), cudaHostAllocMapped), "progress word");
+        h[0] = h[1] = 0u;
         if (cudaHostGetDevicePointer(&dptr, h, 0) != cudaSuccess) {
             cudaFreeHost(h);
             fail(MFM_ERR_CUDA, "mapped progress word unavailable");
@@ -1596,6 +1926,11 @@ extern "C" int mfm_dp_destroy(mfm_dp* dp) {
     return guarded([&] {
         if (!dp) return;
         DeviceGuard guard(dp->device);
+        try {  // collective unless aborted: no rank frees its buffer while another maps it
+            dp_sym_release(dp, device_stream(dp->device));
+        } catch (...) {
+            cudaFree(dp->sym);  // the group was aborted meanwhile
+        }
         const ncclComm_t c = dp->comm;
         const bool aborted = dp->aborted;  // an aborted communicator is already released
         cudaFreeHost(dp->prog_h);

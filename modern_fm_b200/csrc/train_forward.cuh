@@ -37,7 +37,40 @@ struct FwdArgs {
     L2Range pre[3];  // row-table path: stage 1's sorted (key, row, x) of this batch
     T* tab;   // row table (nrows, TW = k): S per row (binary FM row-table path; g in grow)
     int TW;
+    // parameter-sharded training with the exchange over peer memory (PART):
+    // the group's buffers (device memory), this batch's exchange number (its
+    // parity picks the buffer), the stage-1 row table to fill (stride k) and
+    // the progress step
+    const struct ShardXchDev* xch;
+    unsigned long long seq;
+    T* tab_out;
+    unsigned step;
 };
+
+constexpr int kMaxDpRanks = 16;
+// Every rank's exchange buffers as this rank addresses them: the partial row
+// tables (two, alternating by the parity of the exchange number) and the
+// per-block flag arrays, with this rank's own flags, failure words and
+// liveness word.
+struct ShardXchDev {
+    const void* part[2][kMaxDpRanks];
+    const unsigned long long* flags[kMaxDpRanks];
+    unsigned long long* my_flags;
+    unsigned* fail;    // this rank's failure word (device memory)
+    unsigned* fail_h;  // the group's mapped host failure word
+    unsigned* progress;
+    unsigned long long spin;  // polls of about 0.2 us before a wait gives up
+    int N, rank, PW;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 template <class T>
 __device__ __forceinline__ T sigmoid_t(T s) {  // optimizer.rs:28-35
@@ -257,8 +290,114 @@ __device__ __forceinline__ void rows_payload(const FwdArgs<T>& A, int64_t e0, in
     }
 }
 
+// Parameter-sharded training, exchange over peer memory: after this block
+// has written its rows' partial sums [S_r | lin_r - sq_r / 2], it raises its
+// flag to the batch's exchange number, waits until the same block of every
+// other rank has done so (bounded: a wait that gives up sets the failure
+// words, and later exchanges skip at once), sums its rows over the ranks in
+// rank order (the other ranks' rows read over NVLink) and finishes them: S to
+// the stage-1 row table, g = loss'(w0 + sum (lin - sq/2) + |S|^2 / 2) x sw to
+// grow (optimizer.rs:38-43). Every block of the forward's grid is resident at
+// once on every rank (the launch caps the grid), so no wait depends on a block
+// that cannot run. A rank rewrites a table two batches later, after its whole
+// previous forward saw every other rank's flags of that batch, by which time
+// each has finished reading it.
+template <class T, int VEC, int LR>
+__device__ __forceinline__ void shard_block_exchange(const FwdArgs<T>& A, int64_t slot0,
+                                                  int64_t nslots) {
+    __shared__ int s_ok;
+    __shared__ __align__(16) T s_row[(256 / 16) * (32 + 4)];  // slots x PW, PW <= k + VEC
+    constexpr int SPB = 256 / LR;  // row slots per block
+    const ShardXchDev& X = *A.xch;
+    const int K = A.k, PW = X.PW, tid = threadIdx.x;
+    __syncthreads();  // the block's rows are written
+    if (tid == 0) {
+        int ok = *(volatile unsigned*)X.fail == 0u;
+        st_release_sys_u64(X.my_flags + blockIdx.x, A.seq);
+        for (int p = 0; p < X.N && ok; ++p) {
+            if (p == X.rank) continue;
+            unsigned long long it = 0;
+            while (ld_acquire_sys_u64(X.flags[p] + blockIdx.x) < A.seq) {
+                if (++it > X.spin) {
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(200);
+            }
+        }
+        if (!ok) {
+            *(volatile unsigned*)X.fail = 1u;
+            *(volatile unsigned*)X.fail_h = 1u;
+        } else if (blockIdx.x == 0 && X.progress) {
+            *(volatile unsigned*)X.progress = A.step;
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const int par = (int)(A.seq & 1);
+    // this block's row slots: SPB consecutive slots, then every nslots
+    for (int64_t j0 = (slot0 / SPB) * SPB; j0 < A.nrows; j0 += nslots) {
+        const int nr = (int)(A.nrows - j0 < SPB ? A.nrows - j0 : SPB);
+        const int nvec = nr * PW / VEC;
+        for (int f = tid; f < nvec; f += blockDim.x) {  // rows j0.. as 16-byte vectors
+            Vec<T, VEC> acc;
+            for (int p0 = 0; p0 < X.N; p0 += 4) {  // four ranks' loads in flight, then added
+                Vec<T, VEC> v[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (p0 + q < X.N) {
+                        const T* src = static_cast<const T*>(X.part[par][p0 + q]) + j0 * PW +
+                                       (int64_t)f * VEC;
+                        if constexpr (sizeof(T) == 8) {
+                            const double2 w = __ldcv(reinterpret_cast<const double2*>(src));
+                            v[q].v[0] = w.x;
+                            v[q].v[1] = w.y;
+                        } else {
+                            const float4 w = __ldcv(reinterpret_cast<const float4*>(src));
+                            v[q].v[0] = w.x;
+                            v[q].v[1] = w.y;
+                            v[q].v[2] = w.z;
+                            v[q].v[3] = w.w;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (p0 + q < X.N)
+#pragma unroll
+                        for (int u = 0; u < VEC; ++u)
+                            acc.v[u] = (p0 + q == 0) ? v[q].v[u] : acc.v[u] + v[q].v[u];
+            }
+            *reinterpret_cast<Vec<T, VEC>*>(s_row + f * VEC) = acc;
+        }
+        __syncthreads();
+        if (tid < nr) {
+            const int64_t j = j0 + tid;
+            const T* pr = s_row + tid * PW;
+            T ss = T(0);
+            for (int c = 0; c < K; c += VEC) {
+                Vec<T, VEC> sv;
+#pragma unroll
+                for (int u = 0; u < VEC; ++u) {
+                    sv.v[u] = pr[c + u];
+                    ss += sv.v[u] * sv.v[u];
+                }
+                *reinterpret_cast<Vec<T, VEC>*>(A.tab_out + j * K + c) = sv;
+            }
+            const int64_t pos = A.pos0 + j;
+            const T sc = A.w0[0] + (pr[K] + T(0.5) * ss), y = A.y[pos];
+            A.grow[j] = A.sw[pos] * (A.loss == MFM_LOSS_LOGISTIC ? sigmoid_t(sc) - y : sc - y);
+        }
+        __syncthreads();  // s_row is rewritten by the next slots
+    }
+}
+
 // TAB: write the row table (S) and g instead of per-entry payloads.
-template <class T, int VEC, int L, int LR, int CAP, bool TAB = false>
+// PART (with TAB; parameter-sharded training): the row's sums over this
+// rank's keys only, [S | lin - sq / 2] at stride A.TW; no score, no g (both
+// follow from the cross-rank sum of these rows).
+template <class T, int VEC, int L, int LR, int CAP, bool TAB = false, bool PART = false>
 __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t slot0,
                                                     int64_t nslots) {
     using Sh = RowsShape<T, VEC, L, LR, CAP>;
@@ -307,12 +446,12 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
 #pragma unroll
             for (int u = 0; u < VEC; ++u) pair += cache[u] * cache[u];
         }
-        T t = lin + T(0.5) * (pair - sq);
+        T t = PART ? lin - T(0.5) * sq : lin + T(0.5) * (pair - sq);
 #pragma unroll
         for (int o = LR / 2; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
         T g = T(0);
         if (TAB) pdl_wait();  // w0 and the writes below follow the predecessor
-        if (live) {  // loss_grad x sample_weight, optimizer.rs:38-43
+        if (live && !PART) {  // loss_grad x sample_weight, optimizer.rs:38-43
             const T s = A.w0[0] + t, y = A.y[row];
             g = A.sw[row] * (A.loss == MFM_LOSS_LOGISTIC ? sigmoid_t(s) - y : s - y);
             if (rl == 0) A.grow[j] = g;
@@ -326,6 +465,7 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
                     for (int u = 0; u < VEC; ++u) o.v[u] = cache[u];
                     *reinterpret_cast<Vec<T, VEC>*>(tr + l * VEC) = o;
                 }
+                if (PART && rl == 0) tr[A.k] = t;
             }
             continue;
         }
@@ -343,11 +483,12 @@ __device__ __forceinline__ void fm_forward_rows_dev(const FwdArgs<T>& A, int64_t
         }
     }
     if (TAB) pdl_wait();
+    if (PART && A.xch) shard_block_exchange<T, VEC, LR>(A, slot0, nslots);
 }
 
-template <class T, int VEC, int L, int LR, int CAP, bool TAB = false>
+template <class T, int VEC, int L, int LR, int CAP, bool TAB = false, bool PART = false>
 __global__ void __launch_bounds__(256, 2) fm_forward_rows_kernel(FwdArgs<T> A) {
-    fm_forward_rows_dev<T, VEC, L, LR, CAP, TAB>(
+    fm_forward_rows_dev<T, VEC, L, LR, CAP, TAB, PART>(
         A, ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / LR,
         ((int64_t)gridDim.x * blockDim.x) / LR);
 }

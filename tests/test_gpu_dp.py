@@ -1,7 +1,7 @@
-"""Data-parallel training on 2 GPUs (NCCL): binary FM on device arrays
-(mfm_fm_fit_device_dp, the row-table path) and FFM / FwFM / multiclass softmax
-FM / binary FM of other widths from host buffers (mfm_fit_csr_dp, the payload
-path). Every rank ends bitwise equal to the others, and equal to a one-GPU fit
+"""Data-parallel training on 2 GPUs: binary FM on device arrays
+(mfm_fm_fit_device_dp, the row-table path, parameter-sharded by key) and FFM /
+FwFM / multiclass softmax FM / binary FM of other widths from host buffers
+(mfm_fit_csr_dp, the payload path). Every rank ends bitwise equal to the others, and equal to a one-GPU fit
 of the same inputs within the float64 training tolerance (1e-7 relative /
 1e-9 absolute: only the summation order differs — per-rank partial sums, then
 the cross-rank sum)."""
@@ -61,13 +61,15 @@ def _fit(opt, device, group=None, **fit_kw):
                                             ("acc_w", state[1]), ("acc_V", state[2]))}
 
 
-def _worker(rank, world, port, opt, out_dir):
+def _worker(rank, world, port, opt, out_dir, mode="shard"):
     import torch
     import torch.distributed as dist
 
     from modern_fm_b200 import dp
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      MFM_B200_DP_MODE="runs" if mode == "runs" else "shard",
+                      MFM_B200_DP_EXCHANGE="peer" if mode == "shard_peer" else "nccl")
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     group = None
@@ -87,15 +89,20 @@ def _free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("mode", ["shard", "shard_peer", "runs"])
 @pytest.mark.parametrize("opt", ["adagrad", "adam"])
-def test_two_gpu_data_parallel_fit(opt):
+def test_two_gpu_data_parallel_fit(opt, mode):
+    """shard: each rank owns half the keys and the ranks sum the row table
+    with an NCCL allreduce (shard_peer: the forward kernel reads the other
+    rank's rows over NVLink); runs: every rank holds every key and the ranks
+    sum the per-key run sums with NCCL."""
     import torch
     import torch.multiprocessing as mp
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(2, _free_port(), opt, d), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _free_port(), opt, d, mode), nprocs=2, join=True)
         ranks = [dict(np.load(os.path.join(d, f"r{r}.npz"))) for r in range(2)]
     for key in ranks[0]:
         np.testing.assert_array_equal(ranks[0][key], ranks[1][key], err_msg=key)
