@@ -890,7 +890,7 @@ struct Trainer {
                 if (nvec <= 1) MFM_FROWS(1, 16, 48)
                 if (nvec <= 2) MFM_FROWS(2, 16, 48)
                 if (nvec <= 4) MFM_FROWS(4, 16, 48)
-                MFM_FROWS(8, 32, 32)
+                MFM_FROWS(8, 16, 32)
 #undef MFM_FROWS
             }
         }
