@@ -22,18 +22,18 @@
 //      coalesced entries per thread: range check, "greater than the previous
 //      entry unless it starts a row", the narrowed copy). When every row is in
 //      order, the common case, that copy is the result and nothing else runs.
-//   2. otherwise csr_prep_count_kernel (warp per row, rows grid-strided)
+//   2. otherwise csr_prep_sort_kernel (warp per row, rows grid-strided)
 //      writes each row's distinct-column count: rows of up to kShortRow entries
-//      that are out of order are counted in shared memory (first occurrences of
-//      each column); longer ones are listed for the sort. An exclusive scan of
-//      the counts gives the output indptr.
+//      that are out of order are sorted and merged once, into a scratch copy
+//      at their input offsets; longer ones are listed for the sort. An
+//      exclusive scan of the counts gives the output indptr.
 //   3. long unsorted rows only: their narrowed columns are gathered into one
 //      buffer and sorted stably within each row by the segmented radix sort
 //      (segsort.cuh), so equal columns keep their original order.
-//   4. csr_prep_write_kernel (rows of up to kShortRow entries and long rows
-//      already in order) and csr_prep_long_kernel (the sorted rows):
-//      each distinct column is written at its row's output offset plus its
-//      rank, with the float64 sum of its duplicates, narrowed once.
+//   4. csr_prep_place_kernel (in-order rows from the input, short sorted rows
+//      from the scratch) and csr_prep_long_kernel (the long sorted rows): each
+//      distinct column at its row's output offset plus its rank, with the
+//      float64 sum of its duplicates, narrowed once.
 // Every sum has a fixed order, so results are bitwise reproducible.
 #include <algorithm>
 
@@ -191,30 +191,38 @@ __device__ __forceinline__ void warp_sort_row(uint64_t* s, int len, int lane) {
 
 __device__ __forceinline__ uint32_t sorted_col(const uint64_t* s, int e) { return col_of(s[e]); }
 
-// flags[0]: kBad* / kUnsorted bits; flags[1]: number of long unsorted rows.
+// How each row reaches the output (row_kind).
+enum : uint8_t {
+    kRowInOrder = 0,  // strictly increasing: copied from the input as it is
+    kRowSorted = 1,   // short and out of order: sorted, merged rows in the scratch
+    kRowLong = 2,     // long and out of order: sorted by segmented_sort, written by
+                      // csr_prep_long_kernel
+};
+
+// Pass 2 (some row is out of order), warp per row: each row's distinct-column
+// count into cnt[row] and its kind. A short out-of-order row (up to kShortRow
+// entries) is sorted once, here — keys (column, position) in a warp bitonic
+// network in registers — and its distinct columns, ascending, each with the
+// float64 sum of its duplicates in their original order narrowed once, are
+// written to the scratch arrays at the row's input offset. Long out-of-order
+// rows are listed for the segmented sort. Pass 1 has validated the structure
+// and every column. flags[0] gets kUnsorted; flags[1] counts long rows.
 template <class T>
 __global__ void __launch_bounds__(kPrepWarps * 32)
-    csr_prep_count_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
-                          const double* __restrict__ data, int64_t n_rows, int64_t nnz,
-                          int64_t n_features, int32_t* __restrict__ ind_out,
-                          T* __restrict__ dat_out, int64_t* __restrict__ cnt,
-                          int64_t* __restrict__ long_row, int64_t max_long, unsigned* flags) {
+    csr_prep_sort_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
+                         const double* __restrict__ data, int64_t n_rows,
+                         int32_t* __restrict__ tmp_ind, T* __restrict__ tmp_dat,
+                         int64_t* __restrict__ cnt, uint8_t* __restrict__ row_kind,
+                         int64_t* __restrict__ long_row, int64_t max_long, unsigned* flags) {
     __shared__ uint64_t skey[kPrepWarps][kShortRow];
+    __shared__ double sval[kPrepWarps][kShortRow];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
     for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
         const int64_t lo = indptr[r], hi = indptr[r + 1];
-        if (hi < lo || lo < 0 || hi > nnz || (r == 0 && lo != 0) ||
-            (r == n_rows - 1 && hi != nnz)) {
-            if (lane == 0) {
-                atomicOr(flags, hi < lo ? kBadOrder : kBadEnds);
-                cnt[r] = 0;
-            }
-            continue;  // warp-uniform: every lane read the same bounds
-        }
         const int64_t len = hi - lo;
         const bool short_row = len <= kShortRow;
-        bool unsorted = false, bad = false;
+        bool unsorted = false;
         int64_t carry = -1;  // the previous chunk's last column
         for (int64_t base = lo; base < hi; base += 32) {
             const int64_t q = base + lane;
@@ -222,116 +230,92 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
             const int64_t c = in ? indices[q] : 0;
             int64_t prev = __shfl_up_sync(0xffffffffu, c, 1);
             if (lane == 0) prev = carry;
-            bad |= in && (c < 0 || c >= n_features);
             unsorted |= in && q > lo && !(c > prev);
             carry = __shfl_sync(0xffffffffu, c, 31);
-            if (in) {
-                ind_out[q] = (int32_t)c;
-                dat_out[q] = (T)data[q];
-                if (short_row)
-                    skey[wib][q - lo] = ((uint64_t)(uint32_t)c << 32) | (uint64_t)(q - lo);
-            }
-        }
-        bad = __any_sync(0xffffffffu, bad);
-        unsorted = __any_sync(0xffffffffu, unsorted);
-        if (bad) {
-            if (lane == 0) {
-                atomicOr(flags, kBadIndex);
-                cnt[r] = 0;
-            }
-            continue;
-        }
-        int64_t count = len;
-        if (unsorted) {
-            if (short_row) {
-                __syncwarp();
-                warp_sort_row(skey[wib], (int)len, lane);
-                int firsts = 0;  // distinct columns: heads of the sorted row's runs
-                for (int e = lane; e < (int)len; e += 32)
-                    firsts += e == 0 || sorted_col(skey[wib], e) != sorted_col(skey[wib], e - 1);
-                count = warp_sum(firsts);
-            } else {
-                count = 0;  // counted after the sort
-                // at most nnz / (kShortRow + 1) rows fit a valid CSR; rows that
-                // overlap (a decreasing indptr, reported by another row) could
-                // list more, so the slot is bounded
-                if (lane == 0) {
-                    const unsigned slot = atomicAdd(flags + 1, 1u);
-                    if (slot < max_long) long_row[slot] = r;
-                }
-            }
-            if (lane == 0 && !(*(volatile unsigned*)flags & kUnsorted))
-                atomicOr(flags, kUnsorted);  // once set, later rows skip the atomic
-        }
-        __syncwarp();  // skey is rewritten by the next row
-        if (lane == 0) cnt[r] = count;
-    }
-}
-
-// Writes rows of up to kShortRow entries, and longer rows that are already
-// strictly increasing, at their output offsets. Reads the caller's input (the
-// output arrays are being rewritten at shifted offsets by other warps).
-template <class T>
-__global__ void __launch_bounds__(kPrepWarps * 32)
-    csr_prep_write_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
-                          const double* __restrict__ data, int64_t n_rows,
-                          const int64_t* __restrict__ out_ptr, int32_t* __restrict__ ind_out,
-                          T* __restrict__ dat_out) {
-    __shared__ uint64_t skey[kPrepWarps][kShortRow];
-    __shared__ double sval[kPrepWarps][kShortRow];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
-    for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + wib; r < n_rows; r += nwarps) {
-        const int64_t lo = indptr[r], hi = indptr[r + 1], o = out_ptr[r];
-        const int64_t len = hi - lo;
-        // strictly increasing rows are copied as they are
-        bool unsorted = false;
-        int64_t carry = -1;
-        const bool short_row = len <= kShortRow;
-        // short rows are staged whole; long ones stop at the first disorder
-        for (int64_t base = lo; base < hi && (short_row || !unsorted); base += 32) {
-            const int64_t q = base + lane;
-            const int64_t c = q < hi ? indices[q] : 0;
-            int64_t prev = __shfl_up_sync(0xffffffffu, c, 1);
-            if (lane == 0) prev = carry;
-            unsorted |= __any_sync(0xffffffffu, q < hi && q > lo && !(c > prev));
-            carry = __shfl_sync(0xffffffffu, c, 31);
-            if (short_row && q < hi) {
+            if (in && short_row) {
                 skey[wib][q - lo] = ((uint64_t)(uint32_t)c << 32) | (uint64_t)(q - lo);
                 sval[wib][q - lo] = data[q];
             }
         }
-        if (!unsorted) {
+        unsorted = __any_sync(0xffffffffu, unsorted);
+        int64_t count = len;
+        uint8_t kind = kRowInOrder;
+        if (unsorted && short_row) {
+            kind = kRowSorted;
+            __syncwarp();
+            const uint64_t* sk = skey[wib];
+            warp_sort_row(skey[wib], (int)len, lane);
+            // heads of the sorted runs are the distinct columns in ascending
+            // order; a head's rank is the number of heads before it, and its
+            // sum adds the run's values in their original order
+            int before = 0;
+            for (int base = 0; base < (int)len; base += 32) {
+                const int e = base + lane;
+                const bool head =
+                    e < (int)len && (e == 0 || sorted_col(sk, e) != sorted_col(sk, e - 1));
+                const unsigned hm = __ballot_sync(0xffffffffu, head);
+                if (head) {
+                    const int rank = before + __popc(hm & ((1u << lane) - 1u));
+                    const uint32_t key = sorted_col(sk, e);
+                    double sum = sval[wib][(uint32_t)sk[e]];
+                    for (int e2 = e + 1; e2 < (int)len && sorted_col(sk, e2) == key; ++e2)
+                        sum += sval[wib][(uint32_t)sk[e2]];
+                    tmp_ind[lo + rank] = (int32_t)key;
+                    tmp_dat[lo + rank] = (T)sum;
+                }
+                before += __popc(hm);
+            }
+            count = before;
+        } else if (unsorted) {
+            kind = kRowLong;
+            count = 0;  // counted after the sort
+            // at most nnz / (kShortRow + 1) rows can be long in a valid CSR
+            if (lane == 0) {
+                const unsigned slot = atomicAdd(flags + 1, 1u);
+                if (slot < max_long) long_row[slot] = r;
+            }
+        }
+        if (unsorted && lane == 0 && !(*(volatile unsigned*)flags & kUnsorted))
+            atomicOr(flags, kUnsorted);  // once set, later rows skip the atomic
+        __syncwarp();  // the shared row is rewritten by the next row
+        if (lane == 0) {
+            cnt[r] = count;
+            row_kind[r] = kind;
+        }
+    }
+}
+
+// Pass 3, warp per row: every row at its output offset — in-order rows from
+// the input (narrowed), sorted rows from the scratch; long rows are left to
+// csr_prep_long_kernel.
+template <class T>
+__global__ void __launch_bounds__(kPrepWarps * 32)
+    csr_prep_place_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
+                          const double* __restrict__ data, int64_t n_rows,
+                          const int64_t* __restrict__ out_ptr,
+                          const uint8_t* __restrict__ row_kind,
+                          const int32_t* __restrict__ tmp_ind, const T* __restrict__ tmp_dat,
+                          int32_t* __restrict__ ind_out, T* __restrict__ dat_out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
+    for (int64_t r = (int64_t)blockIdx.x * kPrepWarps + (threadIdx.x >> 5); r < n_rows;
+         r += nwarps) {
+        const uint8_t kind = row_kind[r];
+        if (kind == kRowLong) continue;
+        const int64_t lo = indptr[r], o = out_ptr[r];
+        if (kind == kRowInOrder) {
+            const int64_t len = indptr[r + 1] - lo;
             for (int64_t t = lane; t < len; t += 32) {
                 ind_out[o + t] = (int32_t)indices[lo + t];
                 dat_out[o + t] = (T)data[lo + t];
             }
-            continue;
-        }
-        if (!short_row) continue;  // written by csr_prep_long_kernel from the sorted rows
-        __syncwarp();
-        const uint64_t* sk = skey[wib];
-        warp_sort_row(skey[wib], (int)len, lane);
-        // heads of the sorted runs are the distinct columns in ascending order;
-        // a head's rank is the number of heads before it, and its sum adds the
-        // run's values in their original order, from the first occurrence
-        int before = 0;
-        for (int base = 0; base < (int)len; base += 32) {
-            const int e = base + lane;
-            const bool head = e < (int)len && (e == 0 || sorted_col(sk, e) != sorted_col(sk, e - 1));
-            const unsigned hm = __ballot_sync(0xffffffffu, head);
-            if (head) {
-                const int rank = before + __popc(hm & ((1u << lane) - 1u));
-                const uint32_t key = sorted_col(sk, e);
-                double sum = sval[wib][(uint32_t)sk[e]];
-                for (int e2 = e + 1; e2 < (int)len && sorted_col(sk, e2) == key; ++e2)
-                    sum += sval[wib][(uint32_t)sk[e2]];
-                ind_out[o + rank] = (int32_t)key;
-                dat_out[o + rank] = (T)sum;
+        } else {
+            const int64_t n = out_ptr[r + 1] - o;
+            for (int64_t t = lane; t < n; t += 32) {
+                ind_out[o + t] = tmp_ind[lo + t];
+                dat_out[o + t] = tmp_dat[lo + t];
             }
-            before += __popc(hm);
         }
-        __syncwarp();  // shared rows are rewritten by the next row
     }
 }
 
@@ -433,12 +417,15 @@ int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features,
     // list); counts go straight into indptr_out
     const int64_t max_long = std::min<int64_t>(n_rows, nnz / (kShortRow + 1) + 1);
     DevBuf<int64_t> long_row(device, (size_t)max_long);
+    DevBuf<uint8_t> row_kind(device, (size_t)n_rows);
+    DevBuf<int32_t> tmp_ind(device, (size_t)std::max<int64_t>(1, nnz));
+    DevBuf<T> tmp_dat(device, (size_t)std::max<int64_t>(1, nnz));
     MFM_CUDA(cudaMemsetAsync(flags.ptr, 0, 2 * sizeof(unsigned), s), "memset");
     const unsigned grid = warp_grid(device, n_rows, kPrepWarps, 8);
-    csr_prep_count_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(
-        indptr, indices, data, n_rows, nnz, n_features, ind_out, dat_out, indptr_out,
+    csr_prep_sort_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(
+        indptr, indices, data, n_rows, tmp_ind.ptr, tmp_dat.ptr, indptr_out, row_kind.ptr,
         long_row.ptr, max_long, flags.ptr);
-    MFM_CHECK_LAUNCH("CSR prep count");
+    MFM_CHECK_LAUNCH("CSR prep sort");
     d2h(h, flags.ptr, 2, s, "CSR prep flags");
     MFM_CUDA(cudaStreamSynchronize(s), "CSR prep count");
 
@@ -476,9 +463,10 @@ int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features,
         MFM_CHECK_LAUNCH("CSR prep long count");
     }
     exclusive_scan<int64_t, int64_t>(device, s, indptr_out, n_rows, indptr_out);
-    csr_prep_write_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(indptr, indices, data, n_rows,
-                                                              indptr_out, ind_out, dat_out);
-    MFM_CHECK_LAUNCH("CSR prep write");
+    csr_prep_place_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(
+        indptr, indices, data, n_rows, indptr_out, row_kind.ptr, tmp_ind.ptr, tmp_dat.ptr,
+        ind_out, dat_out);
+    MFM_CHECK_LAUNCH("CSR prep place");
     if (n_long > 0) {
         const unsigned lg = warp_grid(device, n_long, kPrepWarps, 8);
         csr_prep_long_kernel<T, true><<<lg, kPrepWarps * 32, 0, s>>>(
