@@ -131,8 +131,8 @@ __global__ void __launch_bounds__(kFlatNT)
 // exchanged by shuffles and partners in other registers compared in place —
 // no shared-memory traffic. Equal columns keep their original order (the
 // position breaks ties).
-template <int R>
-__device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[R], int lane) {
+template <class K, int R>
+__device__ __forceinline__ void warp_sort_regs(K (&v)[R], int lane) {
 #pragma unroll
     for (int k = 2; k <= 32 * R; k <<= 1) {
 #pragma unroll
@@ -144,7 +144,7 @@ __device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[R], int lane) {
                     if (r & jr) continue;
                     const int e = r * 32 + lane;
                     const bool up = (e & k) == 0;
-                    const uint64_t x = v[r], y = v[r | jr];
+                    const K x = v[r], y = v[r | jr];
                     if ((x > y) == up) {
                         v[r] = y;
                         v[r | jr] = x;
@@ -155,7 +155,7 @@ __device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[R], int lane) {
                 for (int r = 0; r < R; ++r) {
                     const int e = r * 32 + lane;
                     const bool up = (e & k) == 0, lower = (lane & j) == 0;
-                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v[r], j);
+                    const K o = __shfl_xor_sync(0xffffffffu, v[r], j);
                     const bool keep_min = lower == up;
                     v[r] = keep_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
                 }
@@ -164,24 +164,49 @@ __device__ __forceinline__ void warp_sort_regs(uint64_t (&v)[R], int lane) {
     }
 }
 
-__device__ __forceinline__ uint32_t col_of(uint64_t key) { return (uint32_t)(key >> 32); }
+// Sort keys: (column << 32) | position in 64 bits, or (column << 8) | position
+// in 32 bits when every column fits in 24 bits (rows of at most 256 entries,
+// so a position fits in 8): half the shuffles and compares per step.
+template <class K>
+struct SortKey;
+template <>
+struct SortKey<uint64_t> {
+    static constexpr int kPosBits = 32;
+    static constexpr uint64_t kPad = ~0ull;
+};
+template <>
+struct SortKey<uint32_t> {
+    static constexpr int kPosBits = 8;
+    static constexpr uint32_t kPad = ~0u;
+};
+template <class K>
+__device__ __forceinline__ K make_key(int64_t col, int pos) {
+    return ((K)(uint32_t)col << SortKey<K>::kPosBits) | (K)(uint32_t)pos;
+}
+template <class K>
+__device__ __forceinline__ uint32_t col_of(K key) { return (uint32_t)(key >> SortKey<K>::kPosBits); }
+template <class K>
+__device__ __forceinline__ uint32_t pos_of(K key) {
+    return (uint32_t)(key & (((K)1 << SortKey<K>::kPosBits) - 1));
+}
 
 // Sorts the row staged in s[0, len) (len <= kShortRow) and writes it back
 // sorted; registers per lane: 2 keys for rows of up to 64 entries, 8 otherwise.
-__device__ __forceinline__ void warp_sort_row(uint64_t* s, int len, int lane) {
+template <class K>
+__device__ __forceinline__ void warp_sort_row(K* s, int len, int lane) {
     if (len <= 64) {
-        uint64_t v[2];
+        K v[2];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : ~0ull;
-        warp_sort_regs<2>(v, lane);
+        for (int r = 0; r < 2; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : SortKey<K>::kPad;
+        warp_sort_regs<K, 2>(v, lane);
 #pragma unroll
         for (int r = 0; r < 2; ++r)
             if (r * 32 + lane < len) s[r * 32 + lane] = v[r];
     } else {
-        uint64_t v[8];
+        K v[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : ~0ull;
-        warp_sort_regs<8>(v, lane);
+        for (int r = 0; r < 8; ++r) v[r] = r * 32 + lane < len ? s[r * 32 + lane] : SortKey<K>::kPad;
+        warp_sort_regs<K, 8>(v, lane);
 #pragma unroll
         for (int r = 0; r < 8; ++r)
             if (r * 32 + lane < len) s[r * 32 + lane] = v[r];
@@ -189,7 +214,8 @@ __device__ __forceinline__ void warp_sort_row(uint64_t* s, int len, int lane) {
     __syncwarp();
 }
 
-__device__ __forceinline__ uint32_t sorted_col(const uint64_t* s, int e) { return col_of(s[e]); }
+template <class K>
+__device__ __forceinline__ uint32_t sorted_col(const K* s, int e) { return col_of(s[e]); }
 
 // How each row reaches the output (row_kind).
 enum : uint8_t {
@@ -206,15 +232,16 @@ enum : uint8_t {
 // float64 sum of its duplicates in their original order narrowed once, are
 // written to the scratch arrays at the row's input offset. Long out-of-order
 // rows are listed for the segmented sort. Pass 1 has validated the structure
-// and every column. flags[0] gets kUnsorted; flags[1] counts long rows.
-template <class T>
+// and every column. flags[0] gets kUnsorted; flags[1] counts long rows. K:
+// the sort key type (uint32_t when the columns fit in 24 bits).
+template <class T, class K>
 __global__ void __launch_bounds__(kPrepWarps * 32)
     csr_prep_sort_kernel(const int64_t* __restrict__ indptr, const int64_t* __restrict__ indices,
                          const double* __restrict__ data, int64_t n_rows,
                          int32_t* __restrict__ tmp_ind, T* __restrict__ tmp_dat,
                          int64_t* __restrict__ cnt, uint8_t* __restrict__ row_kind,
                          int64_t* __restrict__ long_row, int64_t max_long, unsigned* flags) {
-    __shared__ uint64_t skey[kPrepWarps][kShortRow];
+    __shared__ K skey[kPrepWarps][kShortRow];
     __shared__ double sval[kPrepWarps][kShortRow];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int64_t nwarps = (int64_t)gridDim.x * kPrepWarps;
@@ -233,7 +260,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
             unsorted |= in && q > lo && !(c > prev);
             carry = __shfl_sync(0xffffffffu, c, 31);
             if (in && short_row) {
-                skey[wib][q - lo] = ((uint64_t)(uint32_t)c << 32) | (uint64_t)(q - lo);
+                skey[wib][q - lo] = make_key<K>(c, (int)(q - lo));
                 sval[wib][q - lo] = data[q];
             }
         }
@@ -243,7 +270,7 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
         if (unsorted && short_row) {
             kind = kRowSorted;
             __syncwarp();
-            const uint64_t* sk = skey[wib];
+            const K* sk = skey[wib];
             warp_sort_row(skey[wib], (int)len, lane);
             // heads of the sorted runs are the distinct columns in ascending
             // order; a head's rank is the number of heads before it, and its
@@ -257,9 +284,9 @@ __global__ void __launch_bounds__(kPrepWarps * 32)
                 if (head) {
                     const int rank = before + __popc(hm & ((1u << lane) - 1u));
                     const uint32_t key = sorted_col(sk, e);
-                    double sum = sval[wib][(uint32_t)sk[e]];
+                    double sum = sval[wib][pos_of(sk[e])];
                     for (int e2 = e + 1; e2 < (int)len && sorted_col(sk, e2) == key; ++e2)
-                        sum += sval[wib][(uint32_t)sk[e2]];
+                        sum += sval[wib][pos_of(sk[e2])];
                     tmp_ind[lo + rank] = (int32_t)key;
                     tmp_dat[lo + rank] = (T)sum;
                 }
@@ -422,9 +449,14 @@ int64_t csr_prep(int device, cudaStream_t s, int64_t n_rows, int64_t n_features,
     DevBuf<T> tmp_dat(device, (size_t)std::max<int64_t>(1, nnz));
     MFM_CUDA(cudaMemsetAsync(flags.ptr, 0, 2 * sizeof(unsigned), s), "memset");
     const unsigned grid = warp_grid(device, n_rows, kPrepWarps, 8);
-    csr_prep_sort_kernel<T><<<grid, kPrepWarps * 32, 0, s>>>(
-        indptr, indices, data, n_rows, tmp_ind.ptr, tmp_dat.ptr, indptr_out, row_kind.ptr,
-        long_row.ptr, max_long, flags.ptr);
+    if (n_features <= ((int64_t)1 << 24))  // column and position in one 32-bit key
+        csr_prep_sort_kernel<T, uint32_t><<<grid, kPrepWarps * 32, 0, s>>>(
+            indptr, indices, data, n_rows, tmp_ind.ptr, tmp_dat.ptr, indptr_out, row_kind.ptr,
+            long_row.ptr, max_long, flags.ptr);
+    else
+        csr_prep_sort_kernel<T, uint64_t><<<grid, kPrepWarps * 32, 0, s>>>(
+            indptr, indices, data, n_rows, tmp_ind.ptr, tmp_dat.ptr, indptr_out, row_kind.ptr,
+            long_row.ptr, max_long, flags.ptr);
     MFM_CHECK_LAUNCH("CSR prep sort");
     d2h(h, flags.ptr, 2, s, "CSR prep flags");
     MFM_CUDA(cudaStreamSynchronize(s), "CSR prep count");

@@ -49,6 +49,20 @@ def test_short_rows_unsorted_with_duplicates(seed):
     _check(ip, ix, dv, 200)
 
 
+@pytest.mark.parametrize("n_features", [(1 << 24) - 1, 1 << 24, (1 << 24) + 1, 1 << 30])
+def test_short_rows_at_the_sort_key_width_boundary(n_features):
+    """Short rows are sorted on 32-bit keys (column << 8 | position) while
+    every column fits in 24 bits and on 64-bit keys beyond; columns at the
+    top of the range, duplicated, on both sides of the switch."""
+    rng = np.random.default_rng(n_features % 1000)
+    lens = [2, 39, 64, 65, 200, 256]
+    top = np.arange(n_features - 40, n_features, dtype=np.int64)
+    ip = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    ix = np.concatenate([rng.choice(top, size=n, replace=True) for n in lens]).astype(np.int64)
+    dv = rng.normal(size=len(ix))
+    _check(ip, ix, dv, n_features)
+
+
 @pytest.mark.parametrize("seed", [0, 1])
 def test_long_rows_unsorted_with_duplicates(seed):
     rng = np.random.default_rng(seed)
