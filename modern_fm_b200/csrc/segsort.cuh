@@ -28,17 +28,23 @@ constexpr int kSortNT = 256;    // threads per tile (= digits per pass)
 constexpr int kSortItems = 16;  // keys per thread
 constexpr int kSortTile = kSortNT * kSortItems;
 
+// Blocks stride over the n_tiles tiles (a grid smaller than n_tiles leaves
+// room on the device for other streams' kernels).
 static __global__ void __launch_bounds__(256)
     seg_hist_kernel(const uint32_t* __restrict__ keys, const int64_t* __restrict__ tile_lo,
-                    const int64_t* __restrict__ tile_hi, int shift,
+                    const int64_t* __restrict__ tile_hi, int64_t n_tiles, int shift,
                     uint32_t* __restrict__ hist) {
     __shared__ uint32_t h[256];
-    h[threadIdx.x] = 0;
-    __syncthreads();
-    const int64_t lo = tile_lo[blockIdx.x], hi = tile_hi[blockIdx.x];
-    for (int64_t p = lo + threadIdx.x; p < hi; p += 256) atomicAdd(&h[(keys[p] >> shift) & 255u], 1u);
-    __syncthreads();
-    hist[(int64_t)blockIdx.x * 256 + threadIdx.x] = h[threadIdx.x];
+    for (int64_t tb = blockIdx.x; tb < n_tiles; tb += gridDim.x) {
+        h[threadIdx.x] = 0;
+        __syncthreads();
+        const int64_t lo = tile_lo[tb], hi = tile_hi[tb];
+        for (int64_t p = lo + threadIdx.x; p < hi; p += 256)
+            atomicAdd(&h[(keys[p] >> shift) & 255u], 1u);
+        __syncthreads();
+        hist[tb * 256 + threadIdx.x] = h[threadIdx.x];
+        __syncthreads();  // h is cleared for the next tile
+    }
 }
 
 // One block (256 threads, thread = digit) per segment; converts the tiles'
@@ -111,7 +117,7 @@ __global__ void __launch_bounds__(kSortNT)
     seg_scatter_kernel(const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin,
                        uint32_t* __restrict__ kout, uint32_t* __restrict__ vout,
                        const int64_t* __restrict__ tile_lo, const int64_t* __restrict__ tile_hi,
-                       const int64_t* __restrict__ tile_seg_lo, int shift,
+                       const int64_t* __restrict__ tile_seg_lo, int64_t n_tiles, int shift,
                        const uint32_t* __restrict__ offs, Out out) {
     constexpr int NW = kSortNT / 32;
     __shared__ uint32_t cnt[NW][256];  // per-warp digit counts -> tile-local start per warp
@@ -119,10 +125,11 @@ __global__ void __launch_bounds__(kSortNT)
     __shared__ uint32_t scan_sm[NW];
     __shared__ uint2 skv[kSortTile];  // (key, value), one 8-byte store per entry
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int64_t lo = tile_lo[blockIdx.x], hi = tile_hi[blockIdx.x];
-    const int64_t seg0 = tile_seg_lo[blockIdx.x];
+    for (int64_t tb = blockIdx.x; tb < n_tiles; tb += gridDim.x) {  // blocks stride over tiles
+    const int64_t lo = tile_lo[tb], hi = tile_hi[tb];
+    const int64_t seg0 = tile_seg_lo[tb];
     for (int i = t; i < NW * 256; i += kSortNT) (&cnt[0][0])[i] = 0;
-    const uint32_t goff = offs[(int64_t)blockIdx.x * 256 + t];
+    const uint32_t goff = offs[tb * 256 + t];
     const int n = (int)(hi - lo), q0 = warp * (32 * kSortItems) + lane;  // tile-local
     const uint32_t* kt = kin + lo;
     const uint32_t* vt = vin + lo;
@@ -188,6 +195,8 @@ __global__ void __launch_bounds__(kSortNT)
             out.store(vout, dst, pay[u]);
         }
     }
+    __syncthreads();  // shared memory is rewritten by the next tile
+    }
 }
 
 // Builds the tile table: segment b = [seg_lo[b], seg_lo[b+1]) gets
@@ -249,14 +258,16 @@ SortResult segmented_sort(int device, cudaStream_t s, uint32_t* k0, uint32_t* v0
     const uint32_t* ki = kfirst ? kfirst : k0;
     uint32_t *vi = v0, *ko = k1, *vo = v1;
     for (int shift = 0; shift < key_bits; shift += 8) {
-        seg_hist_kernel<<<(unsigned)n_tiles, 256, 0, s>>>(ki, tlo.ptr, thi.ptr, shift, hist.ptr);
+        seg_hist_kernel<<<(unsigned)n_tiles, 256, 0, s>>>(ki, tlo.ptr, thi.ptr, n_tiles, shift,
+                                                          hist.ptr);
         seg_offsets_kernel<<<(unsigned)n_seg, 256, 0, s>>>(d_seg_lo, seg_tile.ptr, hist.ptr);
         if (gather && shift + 8 >= key_bits)
             seg_scatter_kernel<Last><<<(unsigned)n_tiles, kSortNT, 0, s>>>(
-                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, shift, hist.ptr, last);
+                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, n_tiles, shift, hist.ptr, last);
         else
             seg_scatter_kernel<PlainValue><<<(unsigned)n_tiles, kSortNT, 0, s>>>(
-                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, shift, hist.ptr, PlainValue{});
+                ki, vi, ko, vo, tlo.ptr, thi.ptr, tseg.ptr, n_tiles, shift, hist.ptr,
+                PlainValue{});
         MFM_CHECK_LAUNCH("segmented sort launch");
         // the next pass reads what this one wrote and writes the other pair
         uint32_t* nk = ko == k1 ? k0 : k1;
@@ -313,12 +324,14 @@ inline void build_sort_tiles(int device, cudaStream_t s, const std::vector<int64
 // segmented_sort restricted to segments [b0, b1) with the epoch tile table T;
 // no host synchronisation. Same buffer rules as segmented_sort. With iota,
 // the values are each entry's position relative to its segment start: the
-// first pass generates them and v0 is not read.
+// first pass generates them and v0 is not read. max_grid > 0 caps the tile
+// kernels' grids (their blocks then stride over the tiles), so that a sort
+// running beside other work leaves room for it.
 template <class Last = PlainValue>
 SortResult segmented_sort_range(cudaStream_t s, const uint32_t* kfirst, uint32_t* k0, uint32_t* v0,
                                 uint32_t* k1, uint32_t* v1, const int64_t* d_seg_lo, int64_t b0,
                                 int64_t b1, SortTiles& T, int key_bits, Last last = Last{},
-                                bool iota = false) {
+                                bool iota = false, unsigned max_grid = 0) {
     SortResult res{k0, v0};
     constexpr bool gather = !std::is_same<Last, PlainValue>::value;
     if (gather && key_bits < 1) key_bits = 1;
@@ -326,28 +339,30 @@ SortResult segmented_sort_range(cudaStream_t s, const uint32_t* kfirst, uint32_t
     const uint32_t* ki = kfirst ? kfirst : k0;
     uint32_t *vi = v0, *ko = k1, *vo = v1;
     if (t1 > t0 && key_bits > 0) {
-        const unsigned nt = (unsigned)(t1 - t0), ns = (unsigned)(b1 - b0);
+        const int64_t ntl = t1 - t0;
+        const unsigned nt = (unsigned)(max_grid > 0 && ntl > (int64_t)max_grid ? max_grid : ntl),
+                       ns = (unsigned)(b1 - b0);
         const int64_t* tlo = T.tlo.ptr + t0;
         const int64_t* thi = T.thi.ptr + t0;
         const int64_t* tsg = T.tseg.ptr + t0;
         uint32_t* hist = T.hist.ptr + t0 * 256;
         for (int shift = 0; shift < key_bits; shift += 8) {
-            seg_hist_kernel<<<nt, 256, 0, s>>>(ki, tlo, thi, shift, hist);
+            seg_hist_kernel<<<nt, 256, 0, s>>>(ki, tlo, thi, ntl, shift, hist);
             seg_offsets_kernel<<<ns, 256, 0, s>>>(d_seg_lo + b0, T.seg_tile.ptr + b0, T.hist.ptr);
             const bool gen = iota && shift == 0;
             if (gather && shift + 8 >= key_bits) {
                 if (gen)
                     seg_scatter_kernel<Last, true><<<nt, kSortNT, 0, s>>>(
-                        ki, vi, ko, vo, tlo, thi, tsg, shift, hist, last);
+                        ki, vi, ko, vo, tlo, thi, tsg, ntl, shift, hist, last);
                 else
                     seg_scatter_kernel<Last><<<nt, kSortNT, 0, s>>>(ki, vi, ko, vo, tlo, thi,
-                                                                    tsg, shift, hist, last);
+                                                                    tsg, ntl, shift, hist, last);
             } else if (gen) {
                 seg_scatter_kernel<PlainValue, true><<<nt, kSortNT, 0, s>>>(
-                    ki, vi, ko, vo, tlo, thi, tsg, shift, hist, PlainValue{});
+                    ki, vi, ko, vo, tlo, thi, tsg, ntl, shift, hist, PlainValue{});
             } else {
                 seg_scatter_kernel<PlainValue><<<nt, kSortNT, 0, s>>>(
-                    ki, vi, ko, vo, tlo, thi, tsg, shift, hist, PlainValue{});
+                    ki, vi, ko, vo, tlo, thi, tsg, ntl, shift, hist, PlainValue{});
             }
             MFM_CHECK_LAUNCH("segmented sort launch");
             uint32_t* nk = ko == k1 ? k0 : k1;

@@ -357,9 +357,19 @@ inline int64_t plan_window() {
     static const int64_t w = [] {
         const char* e = getenv("MFM_B200_PLAN_WINDOW");
         const long long v = e ? atoll(e) : 0;
-        return v > 0 ? (int64_t)v : (int64_t)32;
+        return v > 0 ? (int64_t)v : (int64_t)128;
     }();
     return w;
+}
+
+// Blocks per SM the plan's kernels may take while batches run beside them
+// (MFM_B200_PLAN_BLOCKS_PER_SM, default 4; 0 = uncapped).
+inline int plan_blocks_per_sm() {
+    static const int v = [] {
+        const char* e = getenv("MFM_B200_PLAN_BLOCKS_PER_SM");
+        return e ? atoi(e) : 4;
+    }();
+    return v;
 }
 
 template <class T>
@@ -553,18 +563,20 @@ struct Trainer {
 
     // Row-table path, batches [b0, b1) of epoch e on stream ps: epoch-order
     // CSR entries (pidx, ex) and the sorted (key, row, x) stream.
-    void plan_tab_window(Stream<T>& st_, int e, int64_t b0, int64_t b1, cudaStream_t ps) {
+    void plan_tab_window(Stream<T>& st_, int e, int64_t b0, int64_t b1, cudaStream_t ps,
+                         int per_sm) {
         const int32_t* order = p_order + (int64_t)e * n_rows;
         const int64_t p0 = b0 * B, p1 = std::min(b1 * B, n_rows);
         if (p1 > p0)
-            expand_kernel<T><<<warp_grid(device, p1 - p0, 8, 8), 256, 0, ps>>>(
+            expand_kernel<T><<<warp_grid(device, p1 - p0, 8, per_sm > 0 ? per_sm : 8), 256, 0,
+                               ps>>>(
                 FEAT, order, p_indptr, p_indices, p_fid, (int)F, p0, p1, B, st_.estart.ptr,
                 st_.seg_lo.ptr, st_.pidx.ptr, nullptr, p_data, st_.erx.ptr, st_.ex.ptr);
         MFM_CHECK_LAUNCH("expand");
         SortResult sr = segmented_sort_range(
             ps, st_.pidx.ptr, st_.k0.ptr, st_.v0.ptr, st_.k1.ptr, st_.v1.ptr, st_.seg_lo.ptr, b0,
             b1, st_.tiles, bits_for(st_.n_keys), RecGather<T>{st_.erx.ptr, st_.rx.ptr},
-            /*iota=*/true);
+            /*iota=*/true, per_sm > 0 ? (unsigned)(per_sm * sm_count(device)) : 0u);
         st_.keys = sr.keys;  // the same buffers for every window
         st_.rrow = sr.vals;
     }
@@ -1207,12 +1219,12 @@ struct Trainer {
     // forked from and joined back to s.
     void run_tab(const FwdArgs<T>& base, PhaseTimer& pt) {
         const cudaStream_t caller = s;
-        // MFM_B200_PLAN_OVERLAP=1 runs the plan in windows on a second stream
-        // beside the batches; by default it is one window that precedes the
-        // batches on one stream (the sort's blocks fill every SM, so
-        // overlapping only delays the latency-bound batch kernels).
+        // The plan runs in windows of batches on a second, low-priority stream
+        // beside the batches (the batch kernels are latency-bound and leave
+        // most of the device idle); MFM_B200_PLAN_OVERLAP=0 runs it as one
+        // window before the batches, on their stream.
         const char* ov = getenv("MFM_B200_PLAN_OVERLAP");
-        const bool overlap = ov && *ov == '1' && !dp;
+        const bool overlap = !(ov && *ov == '0') && !dp;
         const cudaStream_t hi = side_stream(device, 0);
         const cudaStream_t lo = overlap ? side_stream(device, 1) : hi;
         std::vector<std::pair<int64_t, int64_t>> win;
@@ -1244,7 +1256,8 @@ struct Trainer {
                 MFM_CUDA(cudaEventRecord(ev_ep, hi), "event");
                 MFM_CUDA(cudaStreamWaitEvent(lo, ev_ep, 0), "event");
                 for (size_t w = 0; w < win.size(); ++w) {
-                    plan_tab_window(S[0], (int)e, win[w].first, win[w].second, lo);
+                    plan_tab_window(S[0], (int)e, win[w].first, win[w].second, lo,
+                                    overlap ? plan_blocks_per_sm() : 0);
                     MFM_CUDA(cudaEventRecord(ev.e[w], lo), "event");
                 }
                 if (dp && !shard) plan_tab_runs(S[0]);
