@@ -1,10 +1,13 @@
-"""The engine's opt-in execution switches change scheduling, not arithmetic:
-a fit under each must equal the default fit bit for bit. The switches are read
-once per process, so every variant runs in its own subprocess.
+"""The engine's execution switches change scheduling, not arithmetic: a fit
+under each must equal the default fit bit for bit. The switches are read once
+per process, so every variant runs in its own subprocess.
 
-  MFM_B200_PDL=0            plain stream order instead of programmatic launch
-  MFM_B200_PLAN_OVERLAP=1   plan windows on a second stream beside the batches
-  MFM_B200_EPOCH_KERNEL=1   one cooperative launch per epoch (payload path)
+  MFM_B200_PDL=0                 plain stream order instead of programmatic launch
+  MFM_B200_PLAN_OVERLAP=0        the plan as one window before the batches, on
+                                 their stream (default: windows on a second stream)
+  MFM_B200_PLAN_WINDOW=2         two-batch plan windows (default 128)
+  MFM_B200_PLAN_BLOCKS_PER_SM=0  uncapped sort grids beside the batches (default 4)
+  MFM_B200_EPOCH_KERNEL=1        one cooperative launch per epoch (payload path)
 """
 
 import os
@@ -74,7 +77,8 @@ def _run(kind, env_extra, d):
     out = os.path.join(d, f"{kind}_{'_'.join(sorted(env_extra)) or 'default'}.npz")
     env = dict(os.environ)
     for key in ("MFM_B200_PDL", "MFM_B200_PLAN_OVERLAP", "MFM_B200_PLAN_WINDOW",
-                "MFM_B200_EPOCH_KERNEL", "MFM_B200_EPOCH_SPIN_LIMIT", "MFM_B200_EPOCH_DROP_BLOCK"):
+                "MFM_B200_PLAN_BLOCKS_PER_SM", "MFM_B200_EPOCH_KERNEL",
+                "MFM_B200_EPOCH_SPIN_LIMIT", "MFM_B200_EPOCH_DROP_BLOCK"):
         env.pop(key, None)
     env.update(env_extra)
     r = subprocess.run([sys.executable, "-c", SCRIPT.format(root=ROOT), kind, out], env=env,
@@ -85,7 +89,9 @@ def _run(kind, env_extra, d):
 
 @pytest.mark.parametrize("kind,env_extra", [
     ("binary", {"MFM_B200_PDL": "0"}),
-    ("binary", {"MFM_B200_PLAN_OVERLAP": "1", "MFM_B200_PLAN_WINDOW": "2"}),
+    ("binary", {"MFM_B200_PLAN_OVERLAP": "0"}),
+    ("binary", {"MFM_B200_PLAN_WINDOW": "2", "MFM_B200_PLAN_BLOCKS_PER_SM": "1"}),
+    ("binary", {"MFM_B200_PLAN_BLOCKS_PER_SM": "0"}),
     ("multiclass", {"MFM_B200_EPOCH_KERNEL": "1"}),
 ])
 def test_switch_is_bitwise_neutral(kind, env_extra):
