@@ -185,6 +185,11 @@ struct VecStep {
                                            const OptDev& o) {
         const T l1 = (T)o.l1[g.reg], l2 = (T)o.l2[g.reg], lr = (T)o.lr;
         const int kind = OPT >= 0 ? OPT : o.kind;
+        // Adam's bias corrections 1 - b^t, computed once per distinct step
+        // count in the vector (a key's coordinates are stepped together, so
+        // their counts normally agree) and reused: the same values either way
+        T t_prev = T(0), bc1 = T(1), bc2 = T(1);
+        bool have_bc = false;
 #pragma unroll
         for (int u = 0; u < VEC; ++u) {
             T th = p.v[u];
@@ -208,8 +213,14 @@ struct VecStep {
                 c.v[u] = t;
                 a.v[u] = m;
                 b.v[u] = v;
-                const T mh = m / (T(1) - exp2(t * (T)o.lb1));  // b1^t
-                const T vh = v / (T(1) - exp2(t * (T)o.lb2));  // b2^t
+                if (!have_bc || t != t_prev) {
+                    bc1 = T(1) - exp2(t * (T)o.lb1);  // b1^t
+                    bc2 = T(1) - exp2(t * (T)o.lb2);  // b2^t
+                    t_prev = t;
+                    have_bc = true;
+                }
+                const T mh = m / bc1;
+                const T vh = v / bc2;
                 th -= lr * mh / (sqrt(vh) + (T)o.eps);
                 break;
             }

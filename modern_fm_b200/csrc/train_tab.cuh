@@ -24,10 +24,12 @@ namespace mfm {
 //
 // Stage 1: one block per chunk of kChunk consecutive sorted entries, one
 // entry per thread; a segmented shuffle reduction per warp, then the warps'
-// pieces of a segment folded in warp order; the owner of a segment (its first
-// entry) applies the optimizer. A segment continued from the previous chunk
-// leaves its sum in ph[chunk]; the last segment, when it continues into the
-// next chunk, leaves its sum in pt[chunk].
+// pieces of a segment folded in warp order at the segment's owner (its first
+// entry). The owners of the runs that end in the chunk hand their sums to
+// shared memory and the whole block applies the optimizer to (run, vector)
+// items. A segment continued from the previous chunk leaves its sum in
+// ph[chunk]; the last segment, when it continues into the next chunk, leaves
+// its sum in pt[chunk].
 // Stage 2: one warp per chunk boundary that starts a crossing run folds
 // pt[first chunk] + ph[...] in chunk order and applies; the last block steps
 // w0. Every sum has a fixed shape, so results are bitwise reproducible.
