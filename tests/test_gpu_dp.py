@@ -113,6 +113,27 @@ def test_two_gpu_data_parallel_fit(opt, mode):
     assert np.abs(ranks[0]["V"] - _data()[3]).max() > 1e-4  # training moved the factors
 
 
+@pytest.mark.parametrize("mode", ["shard", "shard_peer", "runs"])
+def test_one_rank_group_fit(mode):
+    """A group of one rank runs the whole multi-GPU pipeline on one GPU (the
+    restricted CSR, the partial forward, the exchange — an NCCL allreduce over
+    one rank or the forward's own flag and buffer — the finish step and the
+    final gather) and must give the one-GPU fit within the float64 training
+    tolerance."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 1:
+        pytest.skip("needs a GPU")
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_worker, args=(1, _free_port(), "adagrad", d, mode), nprocs=1, join=True)
+        got = dict(np.load(os.path.join(d, "r0.npz")))
+    one = _fit("adagrad", 0)
+    for key in ("w0", "w", "V", "acc_w", "acc_V"):
+        np.testing.assert_allclose(got[key], one[key], rtol=1e-7, atol=1e-9, err_msg=key)
+    assert np.abs(got["V"] - _data()[3]).max() > 1e-4
+
+
 def _lost_peer_worker(rank, world, port, out_dir):
     import time
 
