@@ -371,8 +371,9 @@ int mfm_fm_fit_device(int dtype, int device, const int64_t* indptr, const int32_
  *     the batch's row table (rows x (k + 1) values) with one ncclAllReduce
  *     (or, with MFM_B200_DP_EXCHANGE=peer, the forward kernel reads the other
  *     ranks' rows over NVLink through CUDA IPC mappings, with bounded flag
- *     waits; every rank must run the same GPU model); after the fit one sum over the ranks gives every rank every
- *     key. MFM_B200_DP_MODE=runs selects the second exchange instead;
+ *     waits; every rank must run the same GPU model); after the fit one sum
+ *     over the ranks gives every rank every key. MFM_B200_DP_MODE=runs selects
+ *     the second exchange instead;
  *   every other shape (FFM, FwFM, multiclass, other k): parameters
  *     replicated; each global batch is cut into `world` contiguous row
  *     slices, rank r scores slice r, the per-key gradient sums over the
